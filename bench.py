@@ -1,0 +1,458 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 quantized-linear path (one JSON line on rank 0).
+
+Workload (default, ``llama3_8b_ffn_decode``): Llama-3-8B FFN decode GEMVs over
+GGUF Q4_0 and Q4_1 weights — gate/up W 14336x4096 and down W 4096x14336,
+weights ~N(0, 0.02) quantized with the bit-exact packer, activations ~N(0, 1)
+F32 with M = 1, 4 and 16 rows. One step = all 18 products (2 types x 3 M x
+3 matrices). Every (type, M, matrix) has its own weight copy, so a step
+streams 627 MB of distinct packed weights (> the 126 MB L2) and no launch
+finds its weights in L2.
+
+Metric: GB/s of algorithmic bytes, N*ceil(K/32)*block_bytes + 4*M*K + 4*M*N
+per product, over the whole step.
+  value : device time, weights and activations resident in HBM;
+  e2e   : through the public API with host buffers: every product copies its
+          activations from pinned host memory and its outputs back inside the
+          timed region.
+
+Multi-GPU (torchrun): every rank serves its own independent decode batches
+with its own weight copy (replicas, weak scaling); value = all ranks' bytes /
+max-over-ranks time.
+
+``--impl reference`` times the reference's own CPU implementation
+(LinearDispatch kThreadedSimd from the reference sources built in
+oracle/_ref, else the C port of it) on the same workload, metric and unit.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+Q4_0, Q4_1, Q8_0 = 2, 3, 8
+BLOCK_BYTES = {Q8_0: 34, Q4_0: 18, Q4_1: 20}
+TNAME = {Q8_0: "q8_0", Q4_0: "q4_0", Q4_1: "q4_1"}
+METRIC = "quantized linear GB/s & % HBM peak (decode), TFLOP/s (prefill); tokens/s at 1/2/4/8 GPU"
+UNIT = "GB/s"
+
+WORKLOADS = {
+    "llama3_8b_ffn_decode": {
+        "qtypes": (Q4_0, Q4_1),
+        "ms": (1, 4, 16),
+        "mats": (("gate", 14336, 4096), ("up", 14336, 4096), ("down", 4096, 14336)),
+    },
+}
+
+
+def algo_bytes(q: int, n: int, k: int, m: int) -> int:
+    return n * ((k + 31) // 32) * BLOCK_BYTES[q] + 4 * m * k + 4 * m * n
+
+
+def products(wl: dict):
+    """(qtype, m, name, n, k) for every product of one step, in launch order."""
+    return [(q, m, name, n, k) for q in wl["qtypes"] for m in wl["ms"] for (name, n, k) in wl["mats"]]
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region (NVML, fast polling in a thread).
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {  # NVML clocks-event-reason bits
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device: int):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thr = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # no NVML: report that no clocks were seen
+            self.nvml = None
+            self.error = repr(exc)
+
+    def _run(self):
+        nv = self.nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                break
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.nvml:
+            self._thr = threading.Thread(target=self._run, daemon=True)
+            self._thr.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thr:
+            self._thr.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mhz = [s[0] for s in self.samples]
+        bits = 0
+        for _, r in self.samples:
+            bits |= r
+        names = [n for b, n in self.REASONS.items() if bits & b and n != "gpu_idle"]
+        return {"sm_mhz": int(statistics.median(mhz)), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, rank: int, world: int, local_rank: int) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import mini_ai_b200 as mq
+    from mini_ai_b200 import build as mq_build
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    if not mq.LIB_PATH.exists():
+        mq_build.build()
+    lib = mq.lib()
+    wl = WORKLOADS[args.workload]
+    prods = products(wl)
+    stream = torch.cuda.current_stream(dev)
+    sh = C.c_void_p(stream.cuda_stream)
+
+    # Weights: generated on the device, packed by the bit-exact device quantizer.
+    gen = torch.Generator(device=dev)
+    handles, host_blocks = [], []
+    keep_host = rank == 0 and world == 1 and not args.no_cpu_baseline
+    for i, (q, m, name, n, k) in enumerate(prods):
+        gen.manual_seed(1000 * rank + i)
+        w32 = torch.randn((n, k), generator=gen, device=dev, dtype=torch.float32).mul_(0.02)
+        blocks = torch.empty(lib.mq_quantized_bytes(q, n, k), dtype=torch.uint8, device=dev)
+        rc = lib.mq_quantize_device(local_rank, q, w32.data_ptr(), n, k, blocks.data_ptr(), blocks.numel(), sh)
+        if rc:
+            raise RuntimeError(mq._lib.last_error())
+        del w32
+        handles.append(mq.CudaWeight.from_device_blocks(blocks, q, n, k, device=local_rank, stream=stream))
+        if keep_host:
+            host_blocks.append(blocks.cpu().numpy())
+        del blocks
+    gen.manual_seed(424242 + rank)
+    xs = {(m, k): torch.randn((m, k), generator=gen, device=dev, dtype=torch.float32)
+          for (_, m, _, _, k) in prods}
+    ys = {(m, n): torch.empty((m, n), dtype=torch.float32, device=dev) for (_, m, _, n, _) in prods}
+    calls = [(handles[i].handle, xs[(m, k)].data_ptr(), m, k, ys[(m, n)].data_ptr(), n)
+             for i, (q, m, name, n, k) in enumerate(prods)]
+    bytes_per_step = sum(algo_bytes(q, n, k, m) for (q, m, _, n, k) in prods)
+    linear = lib.mq_linear
+
+    def step(events=None):
+        for j, (h, x, m, k, y, n) in enumerate(calls):
+            if events is not None:
+                events[j].record(stream)
+            rc = linear(h, x, m, k, None, y, n, sh)
+            if rc:
+                raise RuntimeError(mq._lib.last_error())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+
+    # Timed region: exactly K steps; per-product events ride along on the same stream.
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(calls) + 1)] for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = lib.mq_kernel_launches()
+    with ClockSampler(local_rank) as clocks:
+        t0.record(stream)
+        for s in range(args.steps):
+            step(ev[s])
+            ev[s][-1].record(stream)
+        t1.record(stream)
+        barrier()
+    launches = lib.mq_kernel_launches() - launches0
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+
+    # Per-product device time, grouped by kernel class (type, M).
+    per_class: dict[str, float] = {}
+    cls_bytes: dict[str, int] = {}
+    cls_first: dict[str, int] = {}
+    cls_count: dict[str, int] = {}
+    for j, (q, m, name, n, k) in enumerate(prods):
+        c = f"gemv_{TNAME[q]}_m{m}"
+        cls_first.setdefault(c, j)
+        cls_count[c] = cls_count.get(c, 0) + 1
+        cls_bytes[c] = cls_bytes.get(c, 0) + algo_bytes(q, n, k, m)
+        per_class[c] = per_class.get(c, 0.0) + sum(ev[s][j].elapsed_time(ev[s][j + 1]) for s in range(args.steps))
+    class_ms = {c: v / args.steps for c, v in per_class.items()}
+    dominant = max(class_ms, key=class_ms.get)
+    j = cls_first[dominant]
+    q, m, _, n, k = prods[j]
+    dom_launches = cls_count[dominant] * _launches_for(lib, calls[j], sh, torch)
+    dom_bytes_per_launch = cls_bytes[dominant] / dom_launches
+    dom_ms_per_launch = class_ms[dominant] / dom_launches
+    peak, peak_kind = peaks()
+    achieved = dom_bytes_per_launch / (dom_ms_per_launch * 1e-3) / 1e9
+    traffic = _traffic(dominant)
+
+    value = world * bytes_per_step / (ms_per_step * 1e-3) / 1e9
+
+    # End to end through the public API with host buffers (pinned), same stream.
+    hx = {key: t.cpu().pin_memory() for key, t in xs.items()}
+    hy = {key: torch.empty(t.shape, dtype=torch.float32).pin_memory() for key, t in ys.items()}
+    h2d = sum(4 * m * k for (_, m, _, _, k) in prods)
+    d2h = sum(4 * m * n for (_, m, _, n, _) in prods)
+
+    def e2e_step():
+        for i, (q, m, name, n, k) in enumerate(prods):
+            xs[(m, k)].copy_(hx[(m, k)], non_blocking=True)
+            handles[i].linear(xs[(m, k)], out=ys[(m, n)], stream=stream)
+            hy[(m, n)].copy_(ys[(m, n)], non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * bytes_per_step / (e2e_ms / args.steps * 1e-3) / 1e9
+
+    cpu = None
+    if keep_host:
+        cpu = cpu_baseline(prods, host_blocks, {key: t.cpu().numpy() for key, t in xs.items()},
+                           max_seconds=args.cpu_seconds)
+
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (GGUF Q4_0/Q4_1 weights)",
+            "data": "synthetic (seeded N(0,0.02) weights packed bit-exactly, N(0,1) activations)",
+            "config": {"workload": args.workload,
+                       "products": "gate/up 14336x4096, down 4096x14336; Q4_0, Q4_1; M = 1, 4, 16",
+                       "bytes_per_step": bytes_per_step,
+                       "l2": "inputs larger than L2: 627 MB of distinct weights per step",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": traffic, "algorithmic_bytes_per_launch": int(dom_bytes_per_launch),
+                         "ms_per_launch": round(dom_ms_per_launch, 6)},
+            "per_class_ms": {c: round(v, 5) for c, v in sorted(class_ms.items())},
+            "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": round(e2e_ms / args.steps, 6)},
+            "gpu_launches": int(launches),
+            "clocks": clocks.summary(),
+        }
+        if cpu is not None:
+            out["cpu_baseline"] = cpu
+        print(json.dumps(out), flush=True)
+    for h in handles:
+        h.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def _launches_for(lib, call, sh, torch) -> int:
+    """Kernel launches one product issues (read from the library's counter)."""
+    h, x, m, k, y, n = call
+    a = lib.mq_kernel_launches()
+    rc = lib.mq_linear(h, x, m, k, None, y, n, sh)
+    torch.cuda.synchronize()
+    if rc:
+        raise RuntimeError("mq_linear failed")
+    return max(1, int(lib.mq_kernel_launches() - a))
+
+
+def _traffic(kernel_class: str):
+    """DRAM bytes per launch for the kernel class, from the committed ncu summary."""
+    f = ROOT / "profiles" / "dram_traffic.txt"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == kernel_class:
+            try:
+                return int(float(parts[1]))
+            except ValueError:
+                return None
+    return None
+
+
+# ---------------------------------------------------------------------------
+# CPU: the reference's own implementation (oracle/_ref) or its C port.
+# ---------------------------------------------------------------------------
+def _cpu_engine():
+    from oracle import Oracle, Reference, reference_available
+
+    if reference_available():
+        return "reference", Reference()
+    return "port", Oracle()
+
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_run(kind, eng, prods, blocks, xs, threads):
+    """One pass over `prods` on the CPU; returns seconds."""
+    if kind == "reference":
+        ws = [eng.weight(q, blocks[i], n, k) for i, (q, m, name, n, k) in enumerate(prods)]
+        t = time.perf_counter()
+        for i, (q, m, name, n, k) in enumerate(prods):
+            ws[i].linear(xs[(m, k)], threads=threads)
+        dt = time.perf_counter() - t
+        for w in ws:
+            w.close()
+        return dt
+    t = time.perf_counter()
+    for i, (q, m, name, n, k) in enumerate(prods):
+        eng.linear(q, blocks[i], n, k, xs[(m, k)], threads=threads)
+    return time.perf_counter() - t
+
+
+def cpu_baseline(prods, blocks, xs, max_seconds: float = 20.0) -> dict:
+    kind, eng = _cpu_engine()
+    threads = cpu_threads()
+    bytes_step = sum(algo_bytes(q, n, k, m) for (q, m, _, n, k) in prods)
+    reps, total = 0, 0.0
+    while reps < 1 or (total < max_seconds * 0.5 and reps < 5):
+        total += cpu_run(kind, eng, prods, blocks, xs, threads)
+        reps += 1
+    return {"value": round(bytes_step * reps / total / 1e9, 4), "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"{reps} full step(s) of the workload ({len(prods)} products, {bytes_step} algorithmic bytes"
+                      f" each), LinearDispatch kThreadedSimd per activation row with SetMatmulThreads({threads})"
+                      if kind == "reference" else f"{reps} full step(s), C port of QuantizedDotRow, {threads} threads"}
+
+
+def host_workload(prods, seed: int = 0):
+    """Seeded host weights (packed by the reference's own QuantizeTensor in row
+    chunks on threads; packing is row-independent) and activations."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    kind, eng = _cpu_engine()
+    rng = np.random.default_rng(seed)
+    blocks = []
+    for (q, m, name, n, k) in prods:
+        w = rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)
+        chunks = np.array_split(np.arange(n), min(32, n))
+        with ThreadPoolExecutor(max_workers=cpu_threads()) as ex:
+            parts = list(ex.map(lambda r: eng.quantize(q, w[r[0]:r[-1] + 1]), chunks))
+        blocks.append(np.concatenate(parts))
+    xs = {}
+    for (q, m, name, n, k) in prods:
+        if (m, k) not in xs:
+            xs[(m, k)] = rng.standard_normal((m, k), dtype=np.float32)
+    return kind, eng, blocks, xs
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return  # the CPU reference runs once, on rank 0
+    wl = WORKLOADS[args.workload]
+    prods = products(wl)
+    kind, eng, blocks, xs = host_workload(prods)
+    threads = cpu_threads()
+    cpu_run(kind, eng, prods[:1], blocks[:1], xs, threads)  # warm the thread pool and caches
+    # Each step is a bounded sample of the workload: one of its products, in launch order.
+    bytes_all = [algo_bytes(q, n, k, m) for (q, m, _, n, k) in prods]
+    total_b, total_t = 0, 0.0
+    for s in range(args.steps):
+        i = s % len(prods)
+        total_t += cpu_run(kind, eng, [prods[i]], [blocks[i]], xs, threads)
+        total_b += bytes_all[i]
+    value = total_b / total_t / 1e9
+    sample = (f"each step = one of the workload's {len(prods)} products, in launch order; "
+              f"{'reference LinearDispatch kThreadedSimd' if kind == 'reference' else 'C port'}, {threads} threads")
+    out = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(total_t / args.steps * 1e3, 3), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f32 (GGUF Q4_0/Q4_1 weights)",
+           "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)", "impl": "reference",
+           "config": {"workload": args.workload,
+                      "products": "gate/up 14336x4096, down 4096x14336; Q4_0, Q4_1; M = 1, 4, 16",
+                      "parallelism": f"{threads} host threads"},
+           "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": kind,
+                            "sample": sample},
+           "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama3_8b_ffn_decode")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        ap.error("--warmup must be >= 3")
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

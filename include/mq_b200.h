@@ -1,0 +1,140 @@
+/*
+ * mq_b200 — B200 (sm_100a) quantized-linear engine behind a plain C ABI.
+ *
+ * Drop-in device path for mini_ai's quantized linear: y = x · Wᵀ over GGUF
+ * Q8_0 / Q4_0 / Q4_1 weights. Every entry point takes plain pointers and
+ * sizes, returns MQ_OK (0) or a negative MQ_ERR_* code, and leaves a message
+ * in mq_last_error() for the calling thread. No C++ exception crosses this
+ * boundary. Device pointers are CUDA device addresses on the handle's device;
+ * `stream` is a cudaStream_t (NULL = the legacy default stream) and every
+ * device call is stream-ordered and asynchronous unless stated otherwise.
+ *
+ * Reference interfaces replaced (paths in the mini_ai project):
+ *   - QuantizeTensor / TensorFromQuantized / DequantizeTensor,
+ *     include/mini_llama/quantized_tensor.h:21-24
+ *   - QuantizedDotRow, include/mini_llama/quantized_tensor.h:25
+ *   - LinearDispatch (quantized branch), include/mini_llama/matmul_dispatch.h:28
+ *   - CudaModelState::UploadWeight + LinearKernel, src/cuda_backend.cu:94-110,275-283
+ *   - CudaDeviceInfo, include/mini_llama/backend.h:10
+ */
+#ifndef MQ_B200_H_
+#define MQ_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* GGML block types; the numeric values are the reference's QuantType ids
+ * (include/mini_llama/quantized_tensor.h:10 == gguf.h:15-17). */
+enum {
+  MQ_Q4_0 = 2, /* 18-byte block: fp16 d, 16 bytes of nibbles; w = d*(q-8)   */
+  MQ_Q4_1 = 3, /* 20-byte block: fp16 d, fp16 m, 16 bytes;     w = d*q + m   */
+  MQ_Q8_0 = 8  /* 34-byte block: fp16 d, 32 int8;              w = d*q       */
+};
+
+enum {
+  MQ_OK = 0,
+  MQ_ERR_INVALID = -1,     /* bad argument: type, shape, pointer, stride     */
+  MQ_ERR_CUDA = -2,        /* a CUDA runtime call failed                     */
+  MQ_ERR_SIZE = -3,        /* byte count does not match rows x cols x type   */
+  MQ_ERR_NONFINITE = -4,   /* quantize input holds Inf/NaN                   */
+  MQ_ERR_RANGE = -5,       /* quantize scale or min overflows fp16           */
+  MQ_ERR_TIMEOUT = -6,     /* a bounded device wait on a peer ran out        */
+  MQ_ERR_UNSUPPORTED = -7  /* not built for this device / configuration      */
+};
+
+typedef struct mq_weight mq_weight; /* opaque device-resident packed weight */
+
+/* Message for the last failing call on this thread ("" if none). */
+const char *mq_last_error(void);
+
+/* Library version string. */
+const char *mq_version(void);
+
+/* Bytes of the GGUF block stream for a rows x cols matrix: rows *
+ * ceil(cols/32) * {34|18|20}; 0 for an unknown type or a non-positive shape.
+ * Mirrors the size rule of TensorFromQuantized, src/quantized_tensor.cc:88-96. */
+size_t mq_quantized_bytes(int qtype, int rows, int cols);
+
+/* Bit-exact host quantizer: packs a row-major F32 rows x cols matrix into
+ * GGUF blocks exactly as QuantizeTensor does (src/quantized_tensor.cc:104-159),
+ * using `threads` host threads (0 = all hardware threads). Errors:
+ * MQ_ERR_NONFINITE for Inf/NaN input, MQ_ERR_RANGE when a scale or Q4_1 min
+ * overflows fp16, MQ_ERR_SIZE when dst_bytes is not mq_quantized_bytes(). */
+int mq_quantize(int qtype, const float *src, int rows, int cols, void *dst, size_t dst_bytes, int threads);
+
+/* Host decoder, DequantizeTensor (src/quantized_tensor.cc:193-206). */
+int mq_dequantize(int qtype, const void *blocks, size_t nbytes, int rows, int cols, float *dst);
+
+/* Device quantizer: the same bit-exact packing as mq_quantize, run on the GPU
+ * over a device F32 matrix into a device GGUF block buffer. Input errors
+ * (non-finite values, fp16 overflow) are reported when the call returns, so
+ * this call synchronizes `stream`. */
+int mq_quantize_device(int device, int qtype, const float *d_src, int rows, int cols, void *d_dst,
+                       size_t dst_bytes, void *stream);
+
+/* Upload a packed weight. `blocks` is the GGUF block stream (host memory when
+ * blocks_on_device == 0, a device pointer on `device` otherwise) of a rows x
+ * cols matrix. The weight is re-laid out on the device for 16-byte vector
+ * loads (quants and fp16 scales in separate, aligned planes); the number of
+ * bytes per weight is unchanged. Replaces CudaModelState::UploadWeight
+ * (src/cuda_backend.cu:275-283). Synchronizes `stream` before returning. */
+int mq_weight_create(int device, int qtype, int rows, int cols, const void *blocks, size_t nbytes,
+                     int blocks_on_device, void *stream, mq_weight **out);
+
+/* Upload rows [row_begin, row_end) of a rows x cols packed weight as its own
+ * handle: the output-row shard one GPU holds when a projection is split
+ * across GPUs. `blocks` is the FULL matrix's block stream (host or device). */
+int mq_weight_shard_create(int device, int qtype, int rows, int cols, int row_begin, int row_end,
+                           const void *blocks, size_t nbytes, int blocks_on_device, void *stream,
+                           mq_weight **out);
+
+/* Release a handle and its device memory (NULL is a no-op). */
+void mq_weight_destroy(mq_weight *w);
+
+/* Shape, type, device and device bytes of a handle (any out-pointer may be NULL). */
+int mq_weight_info(const mq_weight *w, int *qtype, int *rows, int *cols, int *device, size_t *device_bytes);
+
+/* Write the handle's weight back as a GGUF block stream to host memory
+ * (round-trip check of the device layout). Synchronous. */
+int mq_weight_export(const mq_weight *w, void *dst, size_t dst_bytes);
+
+/* y[i, n] = sum_k x[i, k] * W[n, k] (+ bias[n]) for i in [0, m).
+ * x: device F32 [m, ldx] with ldx >= cols; y: device F32 [m, ldy] with
+ * ldy >= rows; bias: device F32 [rows] or NULL. Small m runs the streaming
+ * GEMV, large m the tcgen05 tensor-core GEMM. Accumulation is fp32; results
+ * match the reference's sequential fp32 dot (QuantizedDotRow,
+ * src/quantized_tensor.cc:161-191) to within accumulation-order rounding.
+ * The quantized branch of LinearDispatch (src/matmul_optimized.cc:172-174)
+ * and LinearKernel (src/cuda_backend.cu:94-110) accept m == 1 only; here any
+ * m >= 0 works (m == 0 is a no-op). */
+int mq_linear(const mq_weight *w, const float *x, int m, int ldx, const float *bias, float *y, int ldy,
+              void *stream);
+
+/* Same product for a ragged batch: `offsets` (host, n_seqs + 1 entries,
+ * offsets[0] == 0, non-decreasing) delimits each request's rows inside the
+ * contiguous [offsets[n_seqs], ldx] activation matrix. The rows are
+ * independent, so the result equals mq_linear with m = offsets[n_seqs]; the
+ * offsets are validated and kept for callers that need per-request slices. */
+int mq_linear_ragged(const mq_weight *w, const float *x, const int *offsets, int n_seqs, int ldx,
+                     const float *bias, float *y, int ldy, void *stream);
+
+/* Kernel selection for the next mq_linear calls on this thread:
+ * 0 = automatic (default), 1 = force the streaming GEMV, 2 = force the
+ * tensor-core GEMM. Returns the previous mode. */
+int mq_set_path(int mode);
+
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads): the evidence a benchmark reports as its kernel count. */
+uint64_t mq_kernel_launches(void);
+
+/* Human-readable device list, like CudaDeviceInfo (src/cuda_backend.cu:355-369). */
+int mq_device_info(char *buf, size_t len);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MQ_B200_H_ */

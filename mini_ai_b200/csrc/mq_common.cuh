@@ -1,0 +1,137 @@
+// Shared definitions for the mq_b200 engine: error state, the device weight
+// layout, fp16 bit conversions, and small PTX helpers for sm_100a.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "mq_b200.h"
+
+namespace mq {
+
+// ---------------------------------------------------------------------------
+// Errors: every entry point returns a code and leaves the message here.
+// ---------------------------------------------------------------------------
+std::string &last_error();
+int fail(int code, const char *fmt, ...);
+int cuda_fail(cudaError_t e, const char *what);
+// Counts every kernel launch issued by the library (mq_kernel_launches).
+void count_launch(int n = 1);
+
+#define MQ_CUDA(call)                                  \
+  do {                                                 \
+    cudaError_t e_ = (call);                           \
+    if (e_ != cudaSuccess) return mq::cuda_fail(e_, #call); \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// GGUF block geometry (src/quantized_tensor.cc:13-23 of the reference).
+// ---------------------------------------------------------------------------
+__host__ __device__ inline int block_bytes(int qtype) {
+  return qtype == MQ_Q8_0 ? 34 : qtype == MQ_Q4_0 ? 18 : qtype == MQ_Q4_1 ? 20 : 0;
+}
+// Quant bytes per 32-weight block in the device layout (scales live apart).
+__host__ __device__ inline int block_qbytes(int qtype) { return qtype == MQ_Q8_0 ? 32 : 16; }
+
+// ---------------------------------------------------------------------------
+// Device-resident weight. The GGUF interleave (2-byte aligned blocks) is split
+// into planes so every load is a naturally aligned vector:
+//   qs : [rows][ld_qs] bytes. Block b of a row at b * block_qbytes. Q8_0 keeps
+//        the 32 int8 in element order; Q4_x keeps the GGUF nibble order (byte
+//        i = element i in the low nibble, element i + 16 in the high nibble).
+//   d  : [rows][ld_s] fp16 scales;   mn : [rows][ld_s] fp16 Q4_1 mins.
+// ld_qs and ld_s are padded so rows start on 16-byte boundaries; the bytes
+// per weight are the GGUF ones (plus at most 15 bytes of padding per row).
+// ---------------------------------------------------------------------------
+struct WeightView {
+  int qtype, rows, cols, nb;   // nb = ceil(cols / 32)
+  const uint8_t *qs;
+  const __half *d, *mn;
+  int64_t ld_qs;               // bytes per row of qs
+  int64_t ld_s;                // halves per row of d / mn
+};
+
+// ---------------------------------------------------------------------------
+// fp16 <-> fp32 by bit manipulation (IEEE binary16, round to nearest even),
+// identical on host and device. Matches the reference's FloatToHalf /
+// HalfToFloat (src/quantized_tensor.cc:46-86) for every non-NaN input and
+// produces the same NaN encodings.
+// ---------------------------------------------------------------------------
+__host__ __device__ inline float bits_f32(uint32_t b) {
+#ifdef __CUDA_ARCH__
+  return __uint_as_float(b);
+#else
+  float f;
+  __builtin_memcpy(&f, &b, 4);
+  return f;
+#endif
+}
+__host__ __device__ inline uint32_t f32_bits(float f) {
+#ifdef __CUDA_ARCH__
+  return __float_as_uint(f);
+#else
+  uint32_t b;
+  __builtin_memcpy(&b, &f, 4);
+  return b;
+#endif
+}
+
+__host__ __device__ inline uint16_t f32_to_f16_rne(float f) {
+  const uint32_t b = f32_bits(f);
+  const uint16_t sign = (uint16_t)((b >> 16) & 0x8000u);
+  const uint32_t e8 = (b >> 23) & 255u, man = b & 0x7fffffu;
+  if (e8 == 255u) return sign | (man ? 0x7e00u : 0x7c00u);
+  const int e = (int)e8 - 112;
+  if (e >= 31) return sign | 0x7c00u;
+  if (e <= 0) {
+    if (e < -10) return sign;
+    const uint32_t sig = man | 0x800000u;
+    const int sh = 14 - e;
+    const uint32_t keep = sig >> sh, rest = sig & ((1u << sh) - 1u), tie = 1u << (sh - 1);
+    return sign | (uint16_t)(keep + ((rest > tie) | ((rest == tie) & (keep & 1u))));
+  }
+  uint32_t keep = man >> 13;
+  const uint32_t rest = man & 0x1fffu;
+  keep += (rest > 0x1000u) | ((rest == 0x1000u) & (keep & 1u));
+  uint32_t ee = (uint32_t)e + (keep >> 10);
+  keep &= 1023u;
+  if (ee >= 31u) return sign | 0x7c00u;
+  return sign | (uint16_t)(ee << 10) | (uint16_t)keep;
+}
+
+__host__ __device__ inline float f16_to_f32(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 31u, f = h & 1023u;
+  if (e == 31u) return f ? bits_f32(0x7fc00000u) : bits_f32(sign | 0x7f800000u);
+  if (e == 0u) return bits_f32(f32_bits((float)f * 5.9604644775390625e-8f) | sign);
+  return bits_f32(sign | ((e + 112u) << 23) | (f << 13));
+}
+
+// ---------------------------------------------------------------------------
+// PTX helpers (sm_100a).
+// ---------------------------------------------------------------------------
+// Streaming 16-byte load that bypasses L1 allocation: weights are read once.
+__device__ __forceinline__ uint4 ld_stream_v4(const void *p) {
+  uint4 v;
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 ld_nc_f4(const float *p) { return __ldg(reinterpret_cast<const float4 *>(p)); }
+
+}  // namespace mq
+
+// Opaque handle behind mq_weight*.
+struct mq_weight {
+  int device = 0;
+  mq::WeightView v{};
+  void *base = nullptr;       // single device allocation holding all planes
+  size_t bytes = 0;
+  int row_begin = 0;          // first row of the full matrix (shards)
+  int full_rows = 0;
+};

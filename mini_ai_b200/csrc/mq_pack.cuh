@@ -1,0 +1,132 @@
+// Weight layout kernels and the bit-exact block quantizer.
+//
+// * repack / unpack: GGUF block stream <-> the device planes of WeightView.
+// * quantize_block : one 32-slot block packed exactly as the reference's
+//   QuantizeTensor (src/quantized_tensor.cc:104-159) packs it. Shared by the
+//   host quantizer (threads over rows) and the device quantizer (one thread
+//   per block), so both produce identical bytes.
+#pragma once
+
+#include <math.h>
+
+#include "mq_common.cuh"
+
+namespace mq {
+
+struct Planes {
+  uint8_t *qs;
+  uint16_t *d, *mn;
+  int64_t ld_qs, ld_s;
+};
+
+// GGUF block stream (rows x nb blocks, starting at `src`) -> device planes.
+__global__ void repack_kernel(const uint8_t *__restrict__ src, int qtype, int rows, int nb, Planes p) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)rows * nb) return;
+  const int64_t r = i / nb, b = i % nb;
+  const int bb = block_bytes(qtype), qb = block_qbytes(qtype), hdr = bb - qb;
+  const uint8_t *blk = src + i * bb;
+  p.d[r * p.ld_s + b] = (uint16_t)(blk[0] | (blk[1] << 8));
+  if (qtype == MQ_Q4_1) p.mn[r * p.ld_s + b] = (uint16_t)(blk[2] | (blk[3] << 8));
+  uint8_t *dst = p.qs + r * p.ld_qs + b * qb;
+  for (int j = 0; j < qb; ++j) dst[j] = blk[hdr + j];
+}
+
+// Device planes -> GGUF block stream (the inverse of repack_kernel).
+__global__ void unpack_kernel(uint8_t *__restrict__ dst, int qtype, int rows, int nb, const Planes p) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)rows * nb) return;
+  const int64_t r = i / nb, b = i % nb;
+  const int bb = block_bytes(qtype), qb = block_qbytes(qtype), hdr = bb - qb;
+  uint8_t *blk = dst + i * bb;
+  const uint16_t d = p.d[r * p.ld_s + b];
+  blk[0] = (uint8_t)(d & 255);
+  blk[1] = (uint8_t)(d >> 8);
+  if (qtype == MQ_Q4_1) {
+    const uint16_t m = p.mn[r * p.ld_s + b];
+    blk[2] = (uint8_t)(m & 255);
+    blk[3] = (uint8_t)(m >> 8);
+  }
+  const uint8_t *q = p.qs + r * p.ld_qs + b * qb;
+  for (int j = 0; j < qb; ++j) blk[hdr + j] = q[j];
+}
+
+// Failure kinds of quantize_block (mapped to MQ_ERR_* and the reference's
+// messages by the callers).
+enum QuantFail { kQuantOk = 0, kQuantNonFinite = 1, kQuantScaleRange = 2, kQuantOffsetRange = 3 };
+
+// Pack one block of `n` (1..32) source values into `blk` (block_bytes(qtype)
+// bytes). Returns a QuantFail.
+//  - statistics start at 0 and cover only the n real values; slots past n
+//    quantize the value 0, like the zero-initialised values[32] the
+//    reference packs (src/quantized_tensor.cc:115-117);
+//  - the signed maximum keeps the first value of largest magnitude;
+//  - scale and Q4_1 min are rounded to fp16 and the rounded values are used;
+//  - q = round-half-away((v - min) / scale) with an IEEE fp32 divide.
+__host__ __device__ inline int quantize_block(int qtype, const float *src, int n, uint8_t *blk) {
+  float v[32];
+  float lo = 0.0f, hi = 0.0f, peak = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float x = j < n ? src[j] : 0.0f;
+    if (!isfinite(x)) return kQuantNonFinite;
+    v[j] = x;
+    lo = x < lo ? x : lo;
+    hi = hi < x ? x : hi;
+    peak = fabsf(x) > fabsf(peak) ? x : peak;
+  }
+  float scale = qtype == MQ_Q8_0 ? fabsf(peak) / 127.0f : qtype == MQ_Q4_0 ? peak / -8.0f : (hi - lo) / 15.0f;
+  const uint16_t sh = f32_to_f16_rne(scale);
+  scale = f16_to_f32(sh);
+  if (!isfinite(scale)) return kQuantScaleRange;
+  blk[0] = (uint8_t)(sh & 255);
+  blk[1] = (uint8_t)(sh >> 8);
+  float zero = 0.0f;
+  if (qtype == MQ_Q4_1) {
+    const uint16_t mh = f32_to_f16_rne(lo);
+    zero = f16_to_f32(mh);
+    if (!isfinite(zero)) return kQuantOffsetRange;
+    blk[2] = (uint8_t)(mh & 255);
+    blk[3] = (uint8_t)(mh >> 8);
+  }
+  int q[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) q[j] = scale == 0.0f ? 0 : (int)roundf((v[j] - zero) / scale);
+  if (qtype == MQ_Q8_0) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) blk[2 + j] = (uint8_t)(int8_t)(q[j] < -127 ? -127 : q[j] > 127 ? 127 : q[j]);
+  } else {
+    const int base = qtype == MQ_Q4_1 ? 4 : 2, zp = qtype == MQ_Q4_0 ? 8 : 0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      int a = q[j] + zp, c = q[j + 16] + zp;
+      a = a < 0 ? 0 : a > 15 ? 15 : a;
+      c = c < 0 ? 0 : c > 15 ? 15 : c;
+      blk[base + j] = (uint8_t)(a | (c << 4));
+    }
+  }
+  return kQuantOk;
+}
+
+// One thread per block. *first_bad (initialised to ~0) receives the smallest
+// (block index << 2 | QuantFail) over failing blocks: the failure of the
+// first bad block in row-major order, where the reference's loop throws.
+__global__ void quantize_kernel(const float *__restrict__ src, int qtype, int rows, int cols, uint8_t *__restrict__ dst,
+                                unsigned long long *first_bad) {
+  const int nb = (cols + 31) >> 5;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)rows * nb) return;
+  const int64_t r = i / nb, b = i % nb;
+  const int c0 = (int)b * 32, n = min(32, cols - c0);
+  uint8_t blk[34];
+  const int rc = quantize_block(qtype, src + r * cols + c0, n, blk);
+  if (rc != kQuantOk) {
+    atomicMin(first_bad, ((unsigned long long)i << 2) | (unsigned long long)rc);
+    return;
+  }
+  const int bb = block_bytes(qtype);
+  uint8_t *out = dst + i * bb;
+  for (int j = 0; j < bb; ++j) out[j] = blk[j];
+}
+
+}  // namespace mq

@@ -1,0 +1,209 @@
+"""GPU parity of the quantized linear against the oracle, through the C ABI.
+
+Every case runs the device path (libmq_b200.so) and compares it with the CPU
+oracle on the same seeded inputs, using the tolerance defined in conftest:
+max|dy|/max|y| <= 1e-4 and |dy_i| <= 1e-4 * sum_k |w_ik x_k| + 1e-6.
+Byte-level results (device layout round trip, device quantizer) must be
+bit-identical.
+"""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+
+from conftest import abs_dot_bound, assert_linear_close, case_names
+from oracle import NAMES, Q4_0, Q4_1, Q8_0, QTYPES
+
+pytestmark = pytest.mark.gpu
+
+THREADS = os.cpu_count() or 1
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def dev(a, device=0):
+    torch = _torch()
+    return torch.from_numpy(np.ascontiguousarray(a)).to(f"cuda:{device}")
+
+
+def gpu_linear(mq, storage, x, device=0, bias=None, path=0):
+    torch = _torch()
+    w = mq.CudaWeight(storage, device=device)
+    prev = mq.set_path(path)
+    try:
+        y = w.linear(dev(x, device), bias=None if bias is None else dev(bias, device))
+        torch.cuda.synchronize(device)
+    finally:
+        mq.set_path(prev)
+    return y.cpu().numpy()
+
+
+@pytest.mark.parametrize("q", QTYPES, ids=lambda q: NAMES[q])
+def test_golden_cases(mq, golden, cuda_device, q):
+    g = golden[q]
+    for name in case_names(g):
+        w, blocks, x, y_ref = g[f"{name}/w"], g[f"{name}/blocks"], g[f"{name}/x"], g[f"{name}/y"]
+        rows, cols = w.shape
+        s = mq.TensorFromQuantized(blocks, rows, cols, q)
+        y = gpu_linear(mq, s, x, cuda_device)
+        assert_linear_close(y, y_ref, abs_dot_bound(g[f"{name}/dequant"], x))
+
+
+@pytest.mark.parametrize("q", QTYPES, ids=lambda q: NAMES[q])
+def test_device_layout_round_trip(mq, golden, cuda_device, q):
+    g = golden[q]
+    for name in case_names(g) + ["edge"]:
+        rows, cols = g[f"{name}/w"].shape
+        blocks = g[f"{name}/blocks"]
+        w = mq.CudaWeight(mq.TensorFromQuantized(blocks, rows, cols, q), device=cuda_device)
+        assert np.array_equal(w.export().bytes, blocks), name
+    rng = np.random.default_rng(3)
+    big = (rng.standard_normal((1024, 4096)) * 0.02).astype(np.float32)
+    s = mq.QuantizeTensor(big, q)
+    assert np.array_equal(mq.CudaWeight(s, device=cuda_device).export().bytes, s.bytes)
+
+
+def _device_quantize(mq, q, w, device):
+    import ctypes as C
+
+    torch = _torch()
+    src = dev(w, device)
+    out = torch.zeros(mq.lib().mq_quantized_bytes(q, *w.shape), dtype=torch.uint8, device=f"cuda:{device}")
+    rc = mq.lib().mq_quantize_device(device, q, src.data_ptr(), w.shape[0], w.shape[1], out.data_ptr(), out.numel(),
+                                     C.c_void_p(torch.cuda.current_stream(device).cuda_stream))
+    return rc, out.cpu().numpy()
+
+
+@pytest.mark.parametrize("q", QTYPES, ids=lambda q: NAMES[q])
+def test_device_quantizer_bit_exact(mq, golden, oracle, cuda_device, q):
+    g = golden[q]
+    for name in case_names(g) + ["edge"]:
+        rc, got = _device_quantize(mq, q, g[f"{name}/w"], cuda_device)
+        assert rc == 0, mq._lib.last_error()
+        assert np.array_equal(got, g[f"{name}/blocks"]), name
+    rng = np.random.default_rng(21 + q)
+    for rows, cols, scale in [(333, 4096, 0.02), (64, 4097, 1e-6), (7, 95, 40.0)]:
+        w = (rng.standard_normal((rows, cols)) * scale).astype(np.float32)
+        w[0, :6] = [0.5, -0.5, 2.5, -0.0, 0.0, -3.5]
+        rc, got = _device_quantize(mq, q, w, cuda_device)
+        assert rc == 0
+        assert np.array_equal(got, mq.QuantizeTensor(w, q).bytes)
+        assert np.array_equal(got, oracle.quantize(q, w))
+
+
+def test_device_quantizer_errors(mq, cuda_device):
+    w = np.zeros((8, 64), np.float32)
+    w[1, 40] = -1.0e5
+    w[6, 3] = np.inf
+    rc, _ = _device_quantize(mq, Q4_1, w, cuda_device)
+    assert rc == mq._lib.MQ_ERR_RANGE and "offset" in mq._lib.last_error()
+    rc, _ = _device_quantize(mq, Q8_0, w, cuda_device)
+    assert rc == mq._lib.MQ_ERR_NONFINITE
+
+
+def _llama_case(mq, oracle, q, rows, cols, m, seed):
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+    s = mq.QuantizeTensor(w, q)
+    x = rng.standard_normal((m, cols)).astype(np.float32)
+    y_ref = oracle.linear(q, s.bytes, rows, cols, x, threads=THREADS)
+    bound = abs_dot_bound(oracle.dequantize(q, s.bytes, rows, cols), x)
+    return s, x, y_ref, bound
+
+
+@pytest.mark.parametrize("q,rows,cols", [(Q8_0, 4096, 4096), (Q4_0, 14336, 4096), (Q4_1, 14336, 4096),
+                                         (Q4_0, 4096, 14336), (Q4_1, 4096, 14336), (Q8_0, 4096, 14336)])
+@pytest.mark.parametrize("m", [1, 4, 16])
+def test_llama_shapes(mq, oracle, cuda_device, q, rows, cols, m):
+    s, x, y_ref, bound = _llama_case(mq, oracle, q, rows, cols, m, seed=rows + cols + m + q)
+    stats = assert_linear_close(gpu_linear(mq, s, x, cuda_device), y_ref, bound)
+    assert stats["max_rel"] < 1e-4
+
+
+@pytest.mark.parametrize("m", [2, 3, 5, 7, 8, 9, 33])
+def test_odd_activation_counts(mq, oracle, cuda_device, m):
+    for q in QTYPES:
+        s, x, y_ref, bound = _llama_case(mq, oracle, q, 300, 4097, m, seed=m * 7 + q)
+        assert_linear_close(gpu_linear(mq, s, x, cuda_device), y_ref, bound)
+
+
+def test_bias_strides_and_alignment(mq, oracle, cuda_device):
+    torch = _torch()
+    q, rows, cols, m = Q4_1, 257, 130, 3
+    s, x, y_ref, bound = _llama_case(mq, oracle, q, rows, cols, m, seed=5)
+    bias = np.linspace(-1, 1, rows).astype(np.float32)
+    w = mq.CudaWeight(s, device=cuda_device)
+    # strided, unaligned activations: x lives at column offset 1 of a wider buffer
+    xbuf = torch.zeros((m, cols + 7), dtype=torch.float32, device=f"cuda:{cuda_device}")
+    xbuf[:, 1:cols + 1] = dev(x, cuda_device)
+    xv = xbuf[:, 1:cols + 1]
+    ybuf = torch.full((m, rows + 5), 7.0, dtype=torch.float32, device=f"cuda:{cuda_device}")
+    w.linear(xv, bias=dev(bias, cuda_device), out=ybuf[:, :rows])
+    torch.cuda.synchronize()
+    got = ybuf.cpu().numpy()
+    assert_linear_close(got[:, :rows], y_ref + bias[None, :], bound + np.abs(bias)[None, :])
+    assert np.all(got[:, rows:] == 7.0)  # nothing written past the output rows
+
+
+def test_sharded_rows_are_slices_of_full(mq, oracle, cuda_device):
+    """A row shard computes exactly the rows of the full matrix (bit-identical)."""
+    torch = _torch()
+    for q in QTYPES:
+        s, x, y_ref, bound = _llama_case(mq, oracle, q, 1024, 512, 2, seed=9 + q)
+        full = mq.CudaWeight(s, device=cuda_device).linear(dev(x, cuda_device)).cpu().numpy()
+        parts = []
+        for g in range(4):
+            sh = mq.CudaWeight(s, device=cuda_device, row_range=(256 * g, 256 * (g + 1)))
+            parts.append(sh.linear(dev(x, cuda_device)).cpu().numpy())
+        torch.cuda.synchronize()
+        assert np.array_equal(np.concatenate(parts, axis=1).view(np.uint32), full.view(np.uint32))
+        assert_linear_close(full, y_ref, bound)
+
+
+def test_ragged_offsets(mq, oracle, cuda_device):
+    import ctypes as C
+
+    torch = _torch()
+    lengths = [1, 7, 33, 64, 2, 5]
+    offsets = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    q = Q8_0
+    s, x, y_ref, bound = _llama_case(mq, oracle, q, 96, 256, int(offsets[-1]), seed=17)
+    w = mq.CudaWeight(s, device=cuda_device)
+    xd = dev(x, cuda_device)
+    y = torch.empty((int(offsets[-1]), 96), dtype=torch.float32, device=f"cuda:{cuda_device}")
+    offs = (C.c_int * len(offsets))(*offsets.tolist())
+    rc = mq.lib().mq_linear_ragged(w.handle, xd.data_ptr(), offs, len(lengths), 256, None, y.data_ptr(), 96,
+                                   C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, mq._lib.last_error()
+    torch.cuda.synchronize()
+    assert_linear_close(y.cpu().numpy(), y_ref, bound)
+    bad = (C.c_int * 3)(0, 5, 4)
+    assert mq.lib().mq_linear_ragged(w.handle, xd.data_ptr(), bad, 2, 256, None, y.data_ptr(), 96, None) == -1
+
+
+def test_deterministic_and_m_zero(mq, oracle, cuda_device):
+    torch = _torch()
+    s, x, _, _ = _llama_case(mq, oracle, Q4_0, 2048, 1024, 4, seed=1)
+    w = mq.CudaWeight(s, device=cuda_device)
+    xd = dev(x, cuda_device)
+    a = w.linear(xd).cpu().numpy()
+    b = w.linear(xd).cpu().numpy()
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    y = torch.full((1, 2048), 3.0, device=f"cuda:{cuda_device}")
+    assert mq.lib().mq_linear(w.handle, xd.data_ptr(), 0, 1024, None, y.data_ptr(), 2048, None) == 0
+    assert float(y[0, 0]) == 3.0
+
+
+def test_dimension_mismatch_raises(mq, cuda_device):
+    s = mq.QuantizeTensor(np.ones((8, 64), np.float32), Q8_0)
+    w = mq.CudaWeight(s, device=cuda_device)
+    torch = _torch()
+    with pytest.raises(RuntimeError, match="dimension mismatch"):
+        w.linear(torch.zeros(63, device=f"cuda:{cuda_device}"))
+    assert "CUDA devices=" in mq.CudaDeviceInfo()
