@@ -66,6 +66,15 @@ def products(wl: dict):
     return [(q, m, name, n, k) for q in wl["qtypes"] for m in wl["ms"] for (name, n, k) in wl["mats"]]
 
 
+def select(prods, only: str | None):
+    """Restrict to products of one type and M, e.g. ``q4_0:16`` (profiling a single kernel class)."""
+    if not only:
+        return prods
+    t, m = only.split(":")
+    q = {v: k for k, v in TNAME.items()}[t]
+    return [p for p in prods if p[0] == q and p[1] == int(m)]
+
+
 def peaks() -> tuple[float, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     try:
@@ -154,14 +163,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         mq_build.build()
     lib = mq.lib()
     wl = WORKLOADS[args.workload]
-    prods = products(wl)
+    prods = select(products(wl), args.only)
     stream = torch.cuda.current_stream(dev)
     sh = C.c_void_p(stream.cuda_stream)
 
     # Weights: generated on the device, packed by the bit-exact device quantizer.
     gen = torch.Generator(device=dev)
     handles, host_blocks = [], []
-    keep_host = rank == 0 and world == 1 and not args.no_cpu_baseline
+    keep_host = rank == 0 and world == 1 and not args.no_cpu_baseline and not args.only
     for i, (q, m, name, n, k) in enumerate(prods):
         gen.manual_seed(1000 * rank + i)
         w32 = torch.randn((n, k), generator=gen, device=dev, dtype=torch.float32).mul_(0.02)
@@ -183,35 +192,48 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     bytes_per_step = sum(algo_bytes(q, n, k, m) for (q, m, _, n, k) in prods)
     linear = lib.mq_linear
 
-    def step(events=None):
+    def step(stream_handle, events=None, s=0):
         for j, (h, x, m, k, y, n) in enumerate(calls):
             if events is not None:
-                events[j].record(stream)
-            rc = linear(h, x, m, k, None, y, n, sh)
+                record_external(events[s][j], stream_handle)
+            rc = linear(h, x, m, k, None, y, n, stream_handle)
             if rc:
                 raise RuntimeError(mq._lib.last_error())
+        if events is not None:
+            record_external(events[s][-1], stream_handle)
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    for _ in range(args.warmup):
-        step()
+    # The timed region replays a CUDA graph holding exactly K steps, captured on
+    # a dedicated stream after eager warm-up on that stream (so per-stream
+    # scratch already exists). External event nodes between the products give
+    # each product's device time inside the timed region.
+    cap = torch.cuda.Stream(dev)
+    cap_h = C.c_void_p(cap.cuda_stream)
+    with torch.cuda.stream(cap):
+        for _ in range(args.warmup):
+            step(cap_h)
     barrier()
-
-    # Timed region: exactly K steps; per-product events ride along on the same stream.
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(calls) + 1)] for _ in range(args.steps)]
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev = [[new_event() for _ in range(len(calls) + 1)] for _ in range(args.steps)]
+    graph = torch.cuda.CUDAGraph()
     launches0 = lib.mq_kernel_launches()
-    with ClockSampler(local_rank) as clocks:
-        t0.record(stream)
+    with torch.cuda.graph(graph, stream=cap):
         for s in range(args.steps):
-            step(ev[s])
-            ev[s][-1].record(stream)
-        t1.record(stream)
+            step(cap_h, ev, s)
+    launches = lib.mq_kernel_launches() - launches0  # kernels inside the timed graph
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(cap):  # replay, and both timing events, on the capture stream
+        graph.replay()  # upload + one untimed pass
         barrier()
-    launches = lib.mq_kernel_launches() - launches0
+        with ClockSampler(local_rank) as clocks:
+            barrier()
+            t0.record(cap)
+            graph.replay()
+            t1.record(cap)
+            barrier()
     ms = t0.elapsed_time(t1)
     if world > 1:
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
@@ -225,11 +247,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     cls_first: dict[str, int] = {}
     cls_count: dict[str, int] = {}
     for j, (q, m, name, n, k) in enumerate(prods):
-        c = f"gemv_{TNAME[q]}_m{m}"
+        c = f"linear_{TNAME[q]}_m{m}"
         cls_first.setdefault(c, j)
         cls_count[c] = cls_count.get(c, 0) + 1
         cls_bytes[c] = cls_bytes.get(c, 0) + algo_bytes(q, n, k, m)
-        per_class[c] = per_class.get(c, 0.0) + sum(ev[s][j].elapsed_time(ev[s][j + 1]) for s in range(args.steps))
+        per_class[c] = per_class.get(c, 0.0) + sum(elapsed_ms(ev[s][j], ev[s][j + 1]) for s in range(args.steps))
     class_ms = {c: v / args.steps for c, v in per_class.items()}
     dominant = max(class_ms, key=class_ms.get)
     j = cls_first[dominant]
@@ -244,6 +266,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     value = world * bytes_per_step / (ms_per_step * 1e-3) / 1e9
 
     # End to end through the public API with host buffers (pinned), same stream.
+    e2e_value, e2e_ms = None, None
     hx = {key: t.cpu().pin_memory() for key, t in xs.items()}
     hy = {key: torch.empty(t.shape, dtype=torch.float32).pin_memory() for key, t in ys.items()}
     h2d = sum(4 * m * k for (_, m, _, _, k) in prods)
@@ -255,21 +278,22 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             handles[i].linear(xs[(m, k)], out=ys[(m, n)], stream=stream)
             hy[(m, n)].copy_(ys[(m, n)], non_blocking=True)
 
-    for _ in range(args.warmup):
-        e2e_step()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record(stream)
-    barrier()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = world * bytes_per_step / (e2e_ms / args.steps * 1e-3) / 1e9
+    if not args.no_e2e:
+        for _ in range(args.warmup):
+            e2e_step()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        barrier()
+        e2e_ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e_value = world * bytes_per_step / (e2e_ms / args.steps * 1e-3) / 1e9
 
     cpu = None
     if keep_host:
@@ -292,8 +316,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                          "traffic": traffic, "algorithmic_bytes_per_launch": int(dom_bytes_per_launch),
                          "ms_per_launch": round(dom_ms_per_launch, 6)},
             "per_class_ms": {c: round(v, 5) for c, v in sorted(class_ms.items())},
-            "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": round(e2e_ms / args.steps, 6)},
+            "e2e": None if e2e_value is None else {
+                "value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms / args.steps, 6)},
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
         }
@@ -304,6 +329,33 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         h.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def new_event():
+    from cuda.bindings import runtime as cudart
+
+    err, ev = cudart.cudaEventCreate()
+    if err != cudart.cudaError_t.cudaSuccess:
+        raise RuntimeError(f"cudaEventCreate: {err}")
+    return ev
+
+
+def record_external(ev, stream_handle) -> None:
+    """Event record node usable for timing inside a captured graph."""
+    from cuda.bindings import runtime as cudart
+
+    (err,) = cudart.cudaEventRecordWithFlags(ev, stream_handle.value, cudart.cudaEventRecordExternal)
+    if err != cudart.cudaError_t.cudaSuccess:
+        raise RuntimeError(f"cudaEventRecordWithFlags: {err}")
+
+
+def elapsed_ms(a, b) -> float:
+    from cuda.bindings import runtime as cudart
+
+    err, ms = cudart.cudaEventElapsedTime(a, b)
+    if err != cudart.cudaError_t.cudaSuccess:
+        raise RuntimeError(f"cudaEventElapsedTime: {err}")
+    return ms
 
 
 def _launches_for(lib, call, sh, torch) -> int:
@@ -442,6 +494,8 @@ def main() -> None:
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama3_8b_ffn_decode")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--only", default=None, help="one kernel class, e.g. q4_0:16 (profiling)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         ap.error("--warmup must be >= 3")

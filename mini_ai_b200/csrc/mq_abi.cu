@@ -15,6 +15,7 @@
 #include "mq_gemm.cuh"
 #include "mq_gemv.cuh"
 #include "mq_pack.cuh"
+#include "mq_tcgemv.cuh"
 
 namespace mq {
 
@@ -81,52 +82,42 @@ int sm_count(int device) {
 }
 
 // ---------------------------------------------------------------------------
-// GEMV launch: M activation rows (1..4 per launch), RPW output rows per CTA.
+// SIMT GEMV launch: M activation rows (1 or 2 per launch), RPW rows per warp.
+// A CTA has 8 warps: warps_k split the K groups, warps_r = 8 / warps_k own
+// different rows.
 // ---------------------------------------------------------------------------
-template <int QT, int M, int RPW, bool VECX>
-cudaError_t launch_gemv_t(const GemvArgs &a, int warps, cudaStream_t s) {
-  const int grid = (a.w.rows + RPW - 1) / RPW;
-  gemv_kernel<QT, M, RPW, VECX><<<grid, warps * 32, 0, s>>>(a);
+template <int QT, int M, int RPW>
+cudaError_t launch_gemv_t(const GemvArgs &a, int warps_k, cudaStream_t s) {
+  const int warps_r = 8 / warps_k;
+  const int rows_per_cta = RPW * warps_r;
+  const int grid = (a.w.rows + rows_per_cta - 1) / rows_per_cta;
+  gemv_kernel<QT, M, RPW><<<grid, 256, 0, s>>>(a, warps_k);
   count_launch();
   return cudaGetLastError();
 }
 
-template <int QT, int M>
-cudaError_t launch_gemv_m(const GemvArgs &a, int rpw, int warps, bool vecx, cudaStream_t s) {
-  if (rpw >= 4) return vecx ? launch_gemv_t<QT, M, 4, true>(a, warps, s) : launch_gemv_t<QT, M, 4, false>(a, warps, s);
-  return vecx ? launch_gemv_t<QT, M, 2, true>(a, warps, s) : launch_gemv_t<QT, M, 2, false>(a, warps, s);
-}
-
 template <int QT>
-cudaError_t launch_gemv_q(const GemvArgs &a, int m, int rpw, int warps, bool vecx, cudaStream_t s) {
-  switch (m) {
-  case 1: return launch_gemv_m<QT, 1>(a, rpw, warps, vecx, s);
-  case 2: return launch_gemv_m<QT, 2>(a, rpw, warps, vecx, s);
-  case 3: return launch_gemv_m<QT, 3>(a, rpw, warps, vecx, s);
-  default: return launch_gemv_m<QT, 4>(a, rpw, warps, vecx, s);
-  }
+cudaError_t launch_gemv_q(const GemvArgs &a, int m, int warps_k, cudaStream_t s) {
+  if (m == 1) return launch_gemv_t<QT, 1, 2>(a, warps_k, s);
+  return launch_gemv_t<QT, 2, 2>(a, warps_k, s);
 }
 
 }  // namespace
 
 int run_gemv(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
              cudaStream_t s) {
-  const bool vecx = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (ldx % 4 == 0);
-  // Warps split the K blocks of a CTA's rows; enough to keep ~8 blocks per lane-slot in flight.
-  const int nb = w->v.nb;
-  int warps = env_int("MQ_GEMV_WARPS", 0);
-  if (warps <= 0) warps = nb >= 256 ? 8 : nb >= 64 ? 4 : nb >= 32 ? 2 : 1;
-  warps = std::min(8, std::max(1, warps));
-  int rpw = env_int("MQ_GEMV_RPW", 0);
-  if (rpw <= 0) rpw = 4;
-  for (int i0 = 0; i0 < m; i0 += 4) {
-    const int mm = std::min(4, m - i0);
+  // K split: enough warps that each lane owns about one 4-block group.
+  int warps_k = env_int("MQ_GEMV_WARPS_K", 0);
+  if (warps_k <= 0) warps_k = std::min(8, std::max(1, (w->v.nb4 + 31) / 32));
+  warps_k = warps_k >= 8 ? 8 : warps_k >= 4 ? 4 : warps_k >= 2 ? 2 : 1;
+  for (int i0 = 0; i0 < m; i0 += 2) {
+    const int mm = std::min(2, m - i0);
     GemvArgs a{w->v, x + (int64_t)i0 * ldx, ldx, bias, y + (int64_t)i0 * ldy, ldy};
     cudaError_t e;
     switch (w->v.qtype) {
-    case MQ_Q8_0: e = launch_gemv_q<MQ_Q8_0>(a, mm, rpw, warps, vecx, s); break;
-    case MQ_Q4_0: e = launch_gemv_q<MQ_Q4_0>(a, mm, rpw, warps, vecx, s); break;
-    default: e = launch_gemv_q<MQ_Q4_1>(a, mm, rpw, warps, vecx, s); break;
+    case MQ_Q8_0: e = launch_gemv_q<MQ_Q8_0>(a, mm, warps_k, s); break;
+    case MQ_Q4_0: e = launch_gemv_q<MQ_Q4_0>(a, mm, warps_k, s); break;
+    default: e = launch_gemv_q<MQ_Q4_1>(a, mm, warps_k, s); break;
     }
     if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
   }
@@ -186,6 +177,8 @@ Planes planes_of(const mq_weight *w) {
 
 }  // namespace
 }  // namespace mq
+
+#include "mq_gemm_host.cuh"
 
 using namespace mq;
 
@@ -284,11 +277,12 @@ int mq_weight_shard_create(int device, int qtype, int rows, int cols, int row_be
   if (g.err != cudaSuccess) return cuda_fail(g.err, "cudaSetDevice");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
-  const int nrows = row_end - row_begin, nb = (cols + 31) / 32, bb = block_bytes(qtype), qb = block_qbytes(qtype);
-  const int64_t ld_qs = (int64_t)nb * qb;                 // multiple of 16 bytes
-  const int64_t ld_s = (int64_t)round_up(nb, 8);           // 16-byte aligned scale rows
-  const size_t qs_bytes = round_up((size_t)nrows * ld_qs, 256);
-  const size_t s_bytes = round_up((size_t)nrows * ld_s * 2, 256);
+  const int nrows = row_end - row_begin, nb = (cols + 31) / 32, bb = block_bytes(qtype);
+  const int nb4 = (nb + 3) / 4, rows_pad = (nrows + 15) / 16 * 16;
+  const int64_t ld_qs = (int64_t)nb4 * group_bytes(qtype);   // multiple of 64 bytes
+  const int64_t ld_s = (int64_t)round_up(4 * nb4, 8);       // 16-byte aligned scale rows
+  const size_t qs_bytes = round_up((size_t)rows_pad * ld_qs, 256);
+  const size_t s_bytes = round_up((size_t)rows_pad * ld_s * 2, 256);
   const size_t total = qs_bytes + s_bytes * (qtype == MQ_Q4_1 ? 2 : 1);
 
   auto *w = new (std::nothrow) mq_weight;
@@ -303,7 +297,7 @@ int mq_weight_shard_create(int device, int qtype, int rows, int cols, int row_be
   }
   w->bytes = total;
   uint8_t *base = static_cast<uint8_t *>(w->base);
-  w->v = WeightView{qtype, nrows, cols, nb, base, reinterpret_cast<const __half *>(base + qs_bytes),
+  w->v = WeightView{qtype, nrows, cols, nb, nb4, rows_pad, base, reinterpret_cast<const __half *>(base + qs_bytes),
                     qtype == MQ_Q4_1 ? reinterpret_cast<const __half *>(base + qs_bytes + s_bytes) : nullptr,
                     ld_qs, ld_s};
   const size_t shard_src_bytes = (size_t)nrows * nb * bb;
@@ -377,7 +371,7 @@ int mq_weight_export(const mq_weight *w, void *dst, size_t dst_bytes) {
 
 int mq_set_path(int mode) {
   const int prev = g_path_mode;
-  if (mode >= 0 && mode <= 2) g_path_mode = mode;
+  if (mode >= 0 && mode <= 4) g_path_mode = mode;
   return prev;
 }
 
@@ -394,9 +388,16 @@ int mq_linear(const mq_weight *w, const float *x, int m, int ldx, const float *b
   if (g.err != cudaSuccess) return cuda_fail(g.err, "cudaSetDevice");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int mode = g_path_mode;
-  const bool use_gemm = mode == 2 || (mode == 0 && m > gemm_min_m(w->v.qtype));
-  if (use_gemm && gemm_supported(w->device)) return run_gemm(w, x, m, ldx, bias, y, ldy, s);
-  return run_gemv(w, x, m, ldx, bias, y, ldy, s);
+  if (mode == 1) return run_gemv(w, x, m, ldx, bias, y, ldy, s);
+  if (mode == 3) return run_tcgemv(w, x, m, ldx, bias, y, ldy, s);
+  if (mode == 4) return run_tcdec(w, x, m, ldx, bias, y, ldy, s);
+  if (mode == 2 || (mode == 0 && m > tcgemv_max_m())) {
+    if (!gemm_supported(w->device))
+      return fail(MQ_ERR_UNSUPPORTED, "the tensor-core GEMM needs an sm_100 device (device %d)", w->device);
+    return run_gemm(w, x, m, ldx, bias, y, ldy, s);
+  }
+  if (m <= simt_max_m()) return run_gemv(w, x, m, ldx, bias, y, ldy, s);
+  return run_tcdec(w, x, m, ldx, bias, y, ldy, s);
 }
 
 int mq_linear_ragged(const mq_weight *w, const float *x, const int *offsets, int n_seqs, int ldx, const float *bias,

@@ -39,22 +39,41 @@ __host__ __device__ inline int block_bytes(int qtype) {
 __host__ __device__ inline int block_qbytes(int qtype) { return qtype == MQ_Q8_0 ? 32 : 16; }
 
 // ---------------------------------------------------------------------------
-// Device-resident weight. The GGUF interleave (2-byte aligned blocks) is split
-// into planes so every load is a naturally aligned vector:
-//   qs : [rows][ld_qs] bytes. Block b of a row at b * block_qbytes. Q8_0 keeps
-//        the 32 int8 in element order; Q4_x keeps the GGUF nibble order (byte
-//        i = element i in the low nibble, element i + 16 in the high nibble).
-//   d  : [rows][ld_s] fp16 scales;   mn : [rows][ld_s] fp16 Q4_1 mins.
-// ld_qs and ld_s are padded so rows start on 16-byte boundaries; the bytes
-// per weight are the GGUF ones (plus at most 15 bytes of padding per row).
+// Device-resident weight ("lane-permuted rows").
+//
+// The GGUF block interleave (2-byte aligned 34/18/20-byte blocks) is split
+// into planes, and the quant bytes of every row are grouped by 4 blocks and
+// permuted so that one aligned 16-byte load hands each consumer exactly the
+// nibbles/bytes it decodes:
+//   qs : [rows_pad][ld_qs] bytes; block group G (blocks 4G..4G+3) of a row
+//        occupies 64 bytes (Q4_x) or 128 bytes (Q8_0) at G * group bytes.
+//        Q4_x: byte 16*t + 4*j + p = quant byte 2t + {0, 8, 1, 9}[p] of block j;
+//        Q8_0: byte 32*t + 8*j + p = quant byte 2t + {0,1,8,9,16,17,24,25}[p].
+//        For t = 0..3 these are the K positions {2t, 2t+1, 2t+8, 2t+9} (+16)
+//        an mma.m16n8k16 fragment lane with threadID_in_group t holds.
+//   d  : [rows_pad][ld_s] fp16 scales;  mn : [rows_pad][ld_s] fp16 Q4_1 mins.
+// Rows are padded to a multiple of 16 and blocks to a multiple of 4 with
+// zero bytes (a zero scale decodes to 0), so tile loops need no bounds
+// checks on loads. Apart from that padding the bytes per weight are the GGUF
+// ones.
 // ---------------------------------------------------------------------------
 struct WeightView {
   int qtype, rows, cols, nb;   // nb = ceil(cols / 32)
+  int nb4, rows_pad;           // ceil(nb / 4), rows rounded up to 16
   const uint8_t *qs;
   const __half *d, *mn;
-  int64_t ld_qs;               // bytes per row of qs
+  int64_t ld_qs;               // bytes per row of qs (nb4 * group bytes)
   int64_t ld_s;                // halves per row of d / mn
 };
+
+__host__ __device__ inline int group_bytes(int qtype) { return qtype == MQ_Q8_0 ? 128 : 64; }
+
+// Position, inside its 4-block group, of quant byte i of block j.
+__host__ __device__ inline int permuted_pos(int qtype, int i, int j) {
+  const int t = (i & 7) >> 1;
+  if (qtype == MQ_Q8_0) return 32 * t + 8 * j + 2 * (i >> 3) + (i & 1);
+  return 16 * t + 4 * j + ((i >> 3) | ((i & 1) << 1));
+}
 
 // ---------------------------------------------------------------------------
 // fp16 <-> fp32 by bit manipulation (IEEE binary16, round to nearest even),
@@ -120,6 +139,11 @@ __device__ __forceinline__ uint4 ld_stream_v4(const void *p) {
   asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint2 ld_stream_v2(const void *p) {
+  uint2 v;
+  asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
   return v;
 }
 __device__ __forceinline__ float4 ld_nc_f4(const float *p) { return __ldg(reinterpret_cast<const float4 *>(p)); }

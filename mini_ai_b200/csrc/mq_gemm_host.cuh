@@ -1,0 +1,375 @@
+// Host side of the tcgen05 GEMM: activation-split workspace, TMA tensor
+// maps, launch configuration and the device error flag.
+#pragma once
+
+#include <cudaTypedefs.h>
+
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "mq_gemm.cuh"
+#include "mq_tcdec.cuh"
+#include "mq_tcgemv.cuh"
+
+namespace mq {
+
+namespace {
+
+// Activation-split workspace, one per (device, stream): calls on one stream
+// are ordered, so they can share it; calls on different streams cannot.
+struct Workspace {
+  void *ptr = nullptr;
+  size_t bytes = 0;
+};
+std::mutex g_ws_mu;
+std::map<std::pair<int, cudaStream_t>, Workspace> g_ws;
+
+int workspace_for(int device, cudaStream_t s, size_t bytes, void **out) {
+  std::lock_guard<std::mutex> lock(g_ws_mu);
+  Workspace &w = g_ws[{device, s}];
+  if (w.bytes < bytes) {
+    if (w.ptr) {
+      // The old buffer may still be read by work queued on this stream.
+      MQ_CUDA(cudaStreamSynchronize(s));
+      MQ_CUDA(cudaFree(w.ptr));
+      w.ptr = nullptr;
+      w.bytes = 0;
+    }
+    const size_t grow = bytes + bytes / 4;
+    MQ_CUDA(cudaMalloc(&w.ptr, grow));
+    w.bytes = grow;
+  }
+  *out = w.ptr;
+  return MQ_OK;
+}
+
+// Split-K fixup tickets, one zeroed array per (device, stream); each launch
+// leaves them at zero again.
+std::map<std::pair<int, cudaStream_t>, Workspace> g_tickets;
+
+int tickets_for(int device, cudaStream_t s, size_t count, int **out) {
+  std::lock_guard<std::mutex> lock(g_ws_mu);
+  Workspace &w = g_tickets[{device, s}];
+  const size_t bytes = count * sizeof(int);
+  if (w.bytes < bytes) {
+    if (w.ptr) {
+      MQ_CUDA(cudaStreamSynchronize(s));
+      MQ_CUDA(cudaFree(w.ptr));
+      w.ptr = nullptr;
+      w.bytes = 0;
+    }
+    MQ_CUDA(cudaMalloc(&w.ptr, bytes));
+    MQ_CUDA(cudaMemsetAsync(w.ptr, 0, bytes, s));
+    w.bytes = bytes;
+  }
+  *out = static_cast<int *>(w.ptr);
+  return MQ_OK;
+}
+
+// Device-visible error flag in mapped pinned host memory, one per device:
+// kernels raise it when a bounded wait runs out; the host reads it without
+// synchronising.
+struct ErrFlag {
+  int *host = nullptr;
+  int *dev = nullptr;
+};
+std::mutex g_err_mu;
+std::map<int, ErrFlag> g_err;
+
+int err_flag(int device, int **dev_ptr, int **host_ptr) {
+  std::lock_guard<std::mutex> lock(g_err_mu);
+  ErrFlag &f = g_err[device];
+  if (!f.host) {
+    MQ_CUDA(cudaHostAlloc(&f.host, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable));
+    *f.host = 0;
+    MQ_CUDA(cudaHostGetDevicePointer(&f.dev, f.host, 0));
+  }
+  *dev_ptr = f.dev;
+  *host_ptr = f.host;
+  return MQ_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int encode_fn(PFN_cuTensorMapEncodeTiled_v12000 *fn) {
+  std::call_once(g_encode_once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (!g_encode) return fail(MQ_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled is not available");
+  *fn = g_encode;
+  return MQ_OK;
+}
+
+// 2-D bf16 tensor map over a [rows, cols] row-major matrix, box [box_rows, 64]
+// with the 128-byte swizzle the UMMA descriptors expect; out-of-range reads
+// return zeros.
+int make_tmap_bf16(CUtensorMap *map, const void *base, int rows, int cols, int box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  int rc = encode_fn(&enc);
+  if (rc) return rc;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kGemmK, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return MQ_OK;
+}
+
+// 2-D tensor map with a 128-byte swizzle over a row-major matrix of `elem`-byte
+// elements: dims {cols, rows}, box {box_cols, box_rows}; out-of-range reads
+// return zeros.
+int make_tmap(CUtensorMap *map, CUtensorMapDataType dtype, int elem, const void *base, int64_t rows, int64_t cols,
+              int64_t row_stride_elems, int box_cols, int box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  int rc = encode_fn(&enc);
+  if (rc) return rc;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(row_stride_elems * elem)};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return MQ_OK;
+}
+
+template <int QT, int BN, int PS, int AS>
+cudaError_t launch_tcdec_t(const CUtensorMap &tq, const CUtensorMap &th, const CUtensorMap &tl, const DecArgs &a,
+                           int tiles, cudaStream_t s) {
+  using L = DecSmem<QT, BN, PS, AS>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e =
+        cudaFuncSetAttribute(tcdec_kernel<QT, BN, PS, AS>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  tcdec_kernel<QT, BN, PS, AS><<<dim3(tiles, a.ksplit), kDecThreads, L::kAlloc, s>>>(tq, th, tl, a);
+  count_launch();
+  return cudaGetLastError();
+}
+
+template <int QT, int BN, int STAGES>
+cudaError_t launch_gemm_t(const CUtensorMap &th, const CUtensorMap &tl, const GemmArgs &a, cudaStream_t s) {
+  using L = GemmSmem<QT, BN, STAGES>;
+  static bool configured = false;  // per process; the attribute applies to every device
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<QT, BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         L::kAlloc);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const dim3 grid((a.w.rows + kGemmRows - 1) / kGemmRows, (a.m + BN - 1) / BN);
+  gemm_kernel<QT, BN, STAGES><<<grid, kGemmThreads, L::kAlloc, s>>>(th, tl, a);
+  count_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int env_threshold(const char *name, int dflt) {
+  const char *e = std::getenv(name);
+  return e && *e ? std::atoi(e) : dflt;
+}
+
+// Largest activation count served by the SIMT GEMV in automatic mode.
+int simt_max_m() {
+  static const int v = env_threshold("MQ_SIMT_MAX_M", 1);
+  return v;
+}
+
+// Largest activation count served by the tensor-core GEMV; above it the
+// tcgen05 GEMM takes over.
+int tcgemv_max_m() {
+  static const int v = std::min(32, env_threshold("MQ_TCGEMV_MAX_M", 32));
+  return v;
+}
+
+bool gemm_supported(int device) {
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess) return false;
+  if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess) return false;
+  return major == 10 && minor == 0;
+}
+
+namespace {
+template <int QT, int NT, int RG>
+cudaError_t launch_tcgemv_t(const TcArgs &a, cudaStream_t s) {
+  constexpr int kWarps = 8;
+  constexpr int smem = kWarps * RG * NT * 4 * 32 * (int)sizeof(float);
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(tcgemv_kernel<QT, NT, RG>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const int grid = (a.w.rows_pad + 16 * RG - 1) / (16 * RG);
+  tcgemv_kernel<QT, NT, RG><<<grid, kWarps * 32, smem, s>>>(a);
+  count_launch();
+  return cudaGetLastError();
+}
+
+template <int QT, int NT>
+cudaError_t launch_tcgemv_n(const TcArgs &a, int rg, cudaStream_t s) {
+  if (rg >= 4 && NT < 4) return launch_tcgemv_t<QT, NT, (NT < 4 ? 4 : 2)>(a, s);  // NT = 4 caps RG at 2 (registers)
+  if (rg >= 2) return launch_tcgemv_t<QT, NT, 2>(a, s);
+  return launch_tcgemv_t<QT, NT, 1>(a, s);
+}
+
+template <int QT>
+cudaError_t launch_tcgemv_q(const TcArgs &a, int nt, int rg, cudaStream_t s) {
+  if (nt == 1) return launch_tcgemv_n<QT, 1>(a, rg, s);
+  if (nt == 2) return launch_tcgemv_n<QT, 2>(a, rg, s);
+  return launch_tcgemv_n<QT, 4>(a, rg, s);
+}
+}  // namespace
+
+// Tensor-core GEMV: up to 32 activation rows per launch (split + kernel).
+int run_tcgemv(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
+               cudaStream_t s) {
+  const WeightView &w = wt->v;
+  const int nbp = 4 * w.nb4;
+  const int sms = 148;
+  for (int i0 = 0; i0 < m; i0 += 32) {
+    const int mm = std::min(32, m - i0);
+    const int nt = mm <= 8 ? 1 : mm <= 16 ? 2 : 4;
+    const size_t xf_bytes = (size_t)nt * nbp * 2 * 32 * 16, xs_bytes = (size_t)nt * nbp * 8 * 4;
+    void *ws = nullptr;
+    int rc = workspace_for(wt->device, s, xf_bytes + xs_bytes + 8 * nt * 4 + 256, &ws);
+    if (rc) return rc;
+    uint4 *xf = static_cast<uint4 *>(ws);
+    float *xsum = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + xf_bytes);
+    float *xinv = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + xf_bytes + xs_bytes);
+    tcx_prep_kernel<<<8 * nt, 256, 0, s>>>(x + (int64_t)i0 * ldx, ldx, mm, w.cols, nbp, xf, xsum, xinv,
+                                           w.qtype == MQ_Q4_1);
+    count_launch();
+    MQ_CUDA(cudaGetLastError());
+    int rg = env_threshold("MQ_TCGEMV_RG", 0);
+    if (rg <= 0) rg = (w.rows_pad / 64 >= 2 * sms) ? 4 : (w.rows_pad / 32 >= 2 * sms) ? 2 : 1;
+    TcArgs a{w, xf, xsum, xinv, mm, bias, y + (int64_t)i0 * ldy, ldy};
+    cudaError_t e;
+    switch (w.qtype) {
+    case MQ_Q8_0: e = launch_tcgemv_q<MQ_Q8_0>(a, nt, rg, s); break;
+    case MQ_Q4_0: e = launch_tcgemv_q<MQ_Q4_0>(a, nt, rg, s); break;
+    default: e = launch_tcgemv_q<MQ_Q4_1>(a, nt, rg, s); break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "tensor-core gemv launch");
+  }
+  return MQ_OK;
+}
+
+// tcgen05 decode GEMM: up to 32 activation rows per launch (split + kernel).
+int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
+              cudaStream_t s) {
+  int *err_dev = nullptr, *err_host = nullptr;
+  int rc = err_flag(wt->device, &err_dev, &err_host);
+  if (rc) return rc;
+  if (*(volatile int *)err_host) {
+    *(volatile int *)err_host = 0;
+    return fail(MQ_ERR_TIMEOUT, "an earlier tensor-core launch on device %d ran out of a bounded wait", wt->device);
+  }
+  const WeightView &w = wt->v;
+  const bool q8 = w.qtype == MQ_Q8_0;
+  const int blocks_per_step = q8 ? 4 : 8;
+  const int steps_total = q8 ? w.nb4 : (w.nb4 + 1) / 2;
+  const int kpad = steps_total * blocks_per_step * 32;
+  const int tiles = (w.rows_pad + kDecRows - 1) / kDecRows;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, wt->device);
+  int ksplit = env_threshold("MQ_TCDEC_KSPLIT", 0);
+  if (ksplit <= 0) ksplit = std::max(1, sms / tiles);  // one wave of one CTA per SM
+  ksplit = std::max(1, std::min(ksplit, steps_total));
+  int *tickets = nullptr;
+  if ((rc = tickets_for(wt->device, s, (size_t)tiles, &tickets))) return rc;
+  for (int i0 = 0; i0 < m; i0 += 32) {
+    const int mm = std::min(32, m - i0);
+    const int bn = mm <= 16 ? 16 : 32;
+    const size_t xbytes = (size_t)bn * kpad * 2;
+    const size_t sbytes = (size_t)(kpad / 32) * bn * 4;
+    const size_t pbytes = ksplit > 1 ? (size_t)ksplit * tiles * kDecRows * bn * 4 : 0;
+    void *ws = nullptr;
+    if ((rc = workspace_for(wt->device, s, 2 * xbytes + sbytes + 256 + pbytes + 1024, &ws))) return rc;
+    uint8_t *base = static_cast<uint8_t *>(ws);
+    __half *xh = reinterpret_cast<__half *>(base);
+    __half *xl = reinterpret_cast<__half *>(base + xbytes);
+    float *xsum = reinterpret_cast<float *>(base + 2 * xbytes);
+    float *xinv = reinterpret_cast<float *>(base + 2 * xbytes + sbytes);
+    float *partial = reinterpret_cast<float *>(base + ((2 * xbytes + sbytes + 256 + 1023) & ~size_t(1023)));
+    dec_prep_kernel<<<bn, 1024, 0, s>>>(x + (int64_t)i0 * ldx, ldx, mm, w.cols, kpad, bn, xh, xl, xsum, xinv,
+                                        w.qtype == MQ_Q4_1);
+    count_launch();
+    MQ_CUDA(cudaGetLastError());
+    CUtensorMap tq, th, tl;
+    if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.qs, w.rows_pad, w.ld_qs, w.ld_qs, 128, kDecRows)))
+      return rc;
+    if ((rc = make_tmap(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, bn, kpad, kpad, 64, bn))) return rc;
+    if ((rc = make_tmap(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xl, bn, kpad, kpad, 64, bn))) return rc;
+    DecArgs a{w, mm, xinv, xsum, bias, y + (int64_t)i0 * ldy, ldy, partial, tickets, ksplit, steps_total, err_dev};
+    cudaError_t e;
+    switch (w.qtype) {
+    case MQ_Q8_0:
+      e = bn == 16 ? launch_tcdec_t<MQ_Q8_0, 16, 3, 4>(tq, th, tl, a, tiles, s)
+                   : launch_tcdec_t<MQ_Q8_0, 32, 3, 4>(tq, th, tl, a, tiles, s);
+      break;
+    case MQ_Q4_0:
+      e = bn == 16 ? launch_tcdec_t<MQ_Q4_0, 16, 4, 4>(tq, th, tl, a, tiles, s)
+                   : launch_tcdec_t<MQ_Q4_0, 32, 4, 4>(tq, th, tl, a, tiles, s);
+      break;
+    default:
+      e = bn == 16 ? launch_tcdec_t<MQ_Q4_1, 16, 4, 4>(tq, th, tl, a, tiles, s)
+                   : launch_tcdec_t<MQ_Q4_1, 32, 4, 4>(tq, th, tl, a, tiles, s);
+      break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "tcgen05 decode launch");
+  }
+  return MQ_OK;
+}
+
+int run_gemm(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
+             cudaStream_t s) {
+  int *err_dev = nullptr, *err_host = nullptr;
+  int rc = err_flag(wt->device, &err_dev, &err_host);
+  if (rc) return rc;
+  if (*(volatile int *)err_host) {
+    *(volatile int *)err_host = 0;
+    return fail(MQ_ERR_TIMEOUT, "an earlier tensor-core GEMM on device %d ran out of a bounded wait", wt->device);
+  }
+  const WeightView &w = wt->v;
+  const int kpad = w.nb * 32;
+  const size_t half = (size_t)m * kpad * sizeof(__nv_bfloat16);
+  void *ws = nullptr;
+  rc = workspace_for(wt->device, s, 2 * half, &ws);
+  if (rc) return rc;
+  __nv_bfloat16 *xh = static_cast<__nv_bfloat16 *>(ws);
+  __nv_bfloat16 *xl = reinterpret_cast<__nv_bfloat16 *>(static_cast<uint8_t *>(ws) + half);
+  const int64_t pairs = (int64_t)m * (kpad / 2);
+  split_x_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, s>>>(x, ldx, m, w.cols, kpad, xh, xl);
+  count_launch();
+  MQ_CUDA(cudaGetLastError());
+
+  constexpr int BN = 256, STAGES = 2;
+  CUtensorMap th, tl;
+  if ((rc = make_tmap_bf16(&th, xh, m, kpad, BN))) return rc;
+  if ((rc = make_tmap_bf16(&tl, xl, m, kpad, BN))) return rc;
+  GemmArgs a{w, y, ldy, bias, m, (w.nb + 1) / 2, err_dev};
+  cudaError_t e;
+  switch (w.qtype) {
+  case MQ_Q8_0: e = launch_gemm_t<MQ_Q8_0, BN, STAGES>(th, tl, a, s); break;
+  case MQ_Q4_0: e = launch_gemm_t<MQ_Q4_0, BN, STAGES>(th, tl, a, s); break;
+  default: e = launch_gemm_t<MQ_Q4_1, BN, STAGES>(th, tl, a, s); break;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+  return MQ_OK;
+}
+
+}  // namespace mq

@@ -1,22 +1,21 @@
-// Streaming quantized GEMV for small activation counts (decode).
+// Streaming SIMT GEMV for one or two activation rows (decode).
 //
-// y[i, n] = sum_b d[n,b] * sum_{j<32} q[n,b,j] * x[i, 32b + j]   (+ m[n,b] * sum_j x)
+// y[i, n] = sum_b d[n,b] * sum_{k<32} q[n,b,k] * x[i, 32b + k]   (+ m[n,b] * sum_k x[i, 32b + k])
 //
-// HBM-bound: each weight byte is read exactly once with a 16-byte
-// L1-bypassing load. A CTA owns RPW consecutive output rows and its warps
-// split the K blocks between them (lane l of warp w takes blocks
-// l + 32*(w + W*j)), so even a 4096-row matrix launches ~1000 CTAs.
-// Each lane decodes whole 32-weight blocks in registers: a nibble or byte is
-// turned into an exact fp32 by splicing it under the exponent of 2^23
-// (byte_perm) and subtracting 2^23 + zero point, then fused-multiply-added
-// into a per-block partial; the fp16 scale (and the Q4_1 min times the block
-// sum of x) is applied once per block. x is read through the read-only path
-// and reused across the RPW rows held in registers. Warps reduce with
-// shuffles, then the CTA combines the warp partials in a fixed order, so the
-// result is deterministic.
+// HBM-bound: every weight byte is read once, 16 bytes per load, bypassing L1.
+// A lane owns whole 4-block groups of a row (64 bytes Q4_x / 128 bytes Q8_0
+// of the lane-permuted layout), so a warp streams 2-4 KB contiguous per row.
+// Each CTA holds RPW rows per warp (x reused from registers across them);
+// the CTA's warps split the groups of K between them when K is long.
+// Decoding stays in registers: a nibble or byte is spliced under the
+// exponent of 2^23 (byte_perm) and 2^23 + zero point is subtracted with a
+// packed fp32 add, then packed fp32 FMAs accumulate a per-block partial; the
+// fp16 scale (and the Q4_1 min times the block sum of x) is applied once per
+// block. Lanes reduce with warp shuffles, warps through shared memory in a
+// fixed order, so results are deterministic.
 //
-// Reference semantics: QuantizedDotRow, src/quantized_tensor.cc:161-191
-// (and LinearKernel, src/cuda_backend.cu:94-110, with its fused bias).
+// Reference semantics: QuantizedDotRow, src/quantized_tensor.cc:161-191, and
+// LinearKernel's fused bias, src/cuda_backend.cu:94-110.
 #pragma once
 
 #include "mq_common.cuh"
@@ -38,150 +37,160 @@ template <> struct Zp<MQ_Q4_0> { static constexpr float kMagic = 8388616.0f; }; 
 template <> struct Zp<MQ_Q4_1> { static constexpr float kMagic = 8388608.0f; };  // 2^23
 template <> struct Zp<MQ_Q8_0> { static constexpr float kMagic = 8388736.0f; };  // 2^23 + 128 (after ^0x80)
 
-// Byte k of `v` spliced under 2^23: the float 2^23 + byte.
-__device__ __forceinline__ float splice(uint32_t v, int k) {
-  return __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7440u | (unsigned)k));
+// Bytes a and b of v, each spliced under 2^23, minus the magic: two exact floats.
+template <int QT>
+__device__ __forceinline__ float2 decode_pair(uint32_t v, int a, int b) {
+  const float2 f = make_float2(__uint_as_float(__byte_perm(v, 0x4B000000u, 0x7440u | (unsigned)a)),
+                               __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7440u | (unsigned)b)));
+  return __fadd2_rn(f, make_float2(-Zp<QT>::kMagic, -Zp<QT>::kMagic));
 }
 
-// x values a lane needs for one 32-element block, loaded per 4-element group.
-template <bool VECX>
-__device__ __forceinline__ float4 load_x4(const float *xr, int k0, int K, bool full) {
-  if (VECX && full) return ld_nc_f4(xr + k0);
-  float4 v;
-  v.x = k0 + 0 < K ? __ldg(xr + k0 + 0) : 0.0f;
-  v.y = k0 + 1 < K ? __ldg(xr + k0 + 1) : 0.0f;
-  v.z = k0 + 2 < K ? __ldg(xr + k0 + 2) : 0.0f;
-  v.w = k0 + 3 < K ? __ldg(xr + k0 + 3) : 0.0f;
-  return v;
-}
-
-__device__ __forceinline__ float dot4(float a0, float a1, float a2, float a3, float4 x, float acc) {
-  acc = fmaf(a0, x.x, acc);
-  acc = fmaf(a1, x.y, acc);
-  acc = fmaf(a2, x.z, acc);
-  acc = fmaf(a3, x.w, acc);
-  return acc;
-}
-
-template <int QT, int M, int RPW, bool VECX>
-__global__ void __launch_bounds__(256) gemv_kernel(const GemvArgs a) {
-  constexpr int QW = QT == MQ_Q8_0 ? 8 : 4;  // 32-bit words of quants per block
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  const int row0 = blockIdx.x * RPW;
+template <int QT, int M, int RPW>
+__global__ void __launch_bounds__(256) gemv_kernel(const GemvArgs a, int warps_k) {
+  constexpr int GW = QT == MQ_Q8_0 ? 32 : 16;  // 32-bit words per row per group
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int wk = warp % warps_k, wr = warp / warps_k, warps_r = (blockDim.x >> 5) / warps_k;
   const WeightView &w = a.w;
-  const int K = w.cols, nb = w.nb, nb_full = w.cols >> 5;
+  const int row0 = (blockIdx.x * warps_r + wr) * RPW;
   const int nrow = min(RPW, w.rows - row0);
+  const int K = w.cols;
 
-  float acc[RPW][M];
+  float2 acc[RPW][M];
 #pragma unroll
   for (int r = 0; r < RPW; ++r)
 #pragma unroll
-    for (int i = 0; i < M; ++i) acc[r][i] = 0.0f;
+    for (int i = 0; i < M; ++i) acc[r][i] = make_float2(0.0f, 0.0f);
 
-  for (int b = lane + 32 * warp; b < nb; b += 32 * nwarps) {
-    uint32_t q[RPW][QW];
-    float dsc[RPW], msc[RPW];
+  if (nrow > 0) {
+    for (int G = lane + 32 * wk; G < w.nb4; G += 32 * warps_k) {
+      uint32_t q[RPW][GW];
+      float dsc[RPW][4], msc[RPW][4];
 #pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-      if (r < nrow) {
-        const uint8_t *p = w.qs + (int64_t)(row0 + r) * w.ld_qs + (int64_t)b * (QW * 4);
+      for (int r = 0; r < RPW; ++r) {
+        const int row = row0 + (r < nrow ? r : 0);
+        const uint8_t *p = w.qs + (int64_t)row * w.ld_qs + (int64_t)G * (GW * 4);
 #pragma unroll
-        for (int h = 0; h < QW / 4; ++h) {
+        for (int h = 0; h < GW / 4; ++h) {
           const uint4 v = ld_stream_v4(p + 16 * h);
           q[r][4 * h + 0] = v.x;
           q[r][4 * h + 1] = v.y;
           q[r][4 * h + 2] = v.z;
           q[r][4 * h + 3] = v.w;
         }
-        dsc[r] = __half2float(w.d[(int64_t)(row0 + r) * w.ld_s + b]);
-        msc[r] = QT == MQ_Q4_1 ? __half2float(w.mn[(int64_t)(row0 + r) * w.ld_s + b]) : 0.0f;
-      } else {
-#pragma unroll
-        for (int h = 0; h < QW; ++h) q[r][h] = 0u;
-        dsc[r] = 0.0f;
-        msc[r] = 0.0f;
-      }
-    }
-    const bool full = b < nb_full;
-    float part[RPW][M], xs[M];
-#pragma unroll
-    for (int i = 0; i < M; ++i) {
-      xs[i] = 0.0f;
-#pragma unroll
-      for (int r = 0; r < RPW; ++r) part[r][i] = 0.0f;
-    }
-    const int kb = b * 32;
-#pragma unroll
-    for (int wd = 0; wd < 4; ++wd) {
-      if constexpr (QT == MQ_Q8_0) {
-        // words 2*wd and 2*wd+1 hold elements 8wd .. 8wd+7
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const int widx = 2 * wd + half;
-          float4 xv[M];
-#pragma unroll
-          for (int i = 0; i < M; ++i) xv[i] = load_x4<VECX>(a.x + (int64_t)i * a.ldx, kb + 4 * widx, K, full);
-#pragma unroll
-          for (int r = 0; r < RPW; ++r) {
-            const uint32_t u = q[r][widx] ^ 0x80808080u;
-            const float v0 = splice(u, 0) - Zp<QT>::kMagic, v1 = splice(u, 1) - Zp<QT>::kMagic;
-            const float v2 = splice(u, 2) - Zp<QT>::kMagic, v3 = splice(u, 3) - Zp<QT>::kMagic;
-#pragma unroll
-            for (int i = 0; i < M; ++i) part[r][i] = dot4(v0, v1, v2, v3, xv[i], part[r][i]);
-          }
+        const uint2 s = *reinterpret_cast<const uint2 *>(w.d + (int64_t)row * w.ld_s + 4 * G);
+        const float2 s01 = __half22float2(*reinterpret_cast<const __half2 *>(&s.x));
+        const float2 s23 = __half22float2(*reinterpret_cast<const __half2 *>(&s.y));
+        const bool live = r < nrow;
+        dsc[r][0] = live ? s01.x : 0.0f;
+        dsc[r][1] = live ? s01.y : 0.0f;
+        dsc[r][2] = live ? s23.x : 0.0f;
+        dsc[r][3] = live ? s23.y : 0.0f;
+        if constexpr (QT == MQ_Q4_1) {
+          const uint2 mm = *reinterpret_cast<const uint2 *>(w.mn + (int64_t)row * w.ld_s + 4 * G);
+          const float2 m01 = __half22float2(*reinterpret_cast<const __half2 *>(&mm.x));
+          const float2 m23 = __half22float2(*reinterpret_cast<const __half2 *>(&mm.y));
+          msc[r][0] = live ? m01.x : 0.0f;
+          msc[r][1] = live ? m01.y : 0.0f;
+          msc[r][2] = live ? m23.x : 0.0f;
+          msc[r][3] = live ? m23.y : 0.0f;
         }
-      } else {
-        // word wd: low nibbles = elements 4wd..4wd+3, high = 16+4wd..16+4wd+3
-        float4 xl[M], xh[M];
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int kb = 32 * (4 * G + j);
+        // x[i, kb .. kb+31] as 8 float4; zero past K (tail and padded blocks)
+        float4 xv[M][8];
 #pragma unroll
         for (int i = 0; i < M; ++i) {
-          xl[i] = load_x4<VECX>(a.x + (int64_t)i * a.ldx, kb + 4 * wd, K, full);
-          xh[i] = load_x4<VECX>(a.x + (int64_t)i * a.ldx, kb + 16 + 4 * wd, K, full);
-          if constexpr (QT == MQ_Q4_1) xs[i] += ((xl[i].x + xl[i].y) + (xl[i].z + xl[i].w)) +
-                                               ((xh[i].x + xh[i].y) + (xh[i].z + xh[i].w));
+          const float *xr = a.x + (int64_t)i * a.ldx + kb;
+          if (kb + 32 <= K && (((uintptr_t)xr) & 15) == 0) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) xv[i][c] = ld_nc_f4(xr + 4 * c);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const int k = kb + 4 * c;
+              xv[i][c] = make_float4(k < K ? __ldg(xr + 4 * c) : 0.0f, k + 1 < K ? __ldg(xr + 4 * c + 1) : 0.0f,
+                                     k + 2 < K ? __ldg(xr + 4 * c + 2) : 0.0f, k + 3 < K ? __ldg(xr + 4 * c + 3) : 0.0f);
+            }
+          }
+        }
+        float xs[M];
+        if constexpr (QT == MQ_Q4_1) {
+#pragma unroll
+          for (int i = 0; i < M; ++i) {
+            float2 s2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              s2 = __fadd2_rn(s2, make_float2(xv[i][c].x, xv[i][c].y));
+              s2 = __fadd2_rn(s2, make_float2(xv[i][c].z, xv[i][c].w));
+            }
+            xs[i] = s2.x + s2.y;
+          }
         }
 #pragma unroll
         for (int r = 0; r < RPW; ++r) {
-          const uint32_t lo = q[r][wd] & 0x0F0F0F0Fu, hi = (q[r][wd] >> 4) & 0x0F0F0F0Fu;
-          const float l0 = splice(lo, 0) - Zp<QT>::kMagic, l1 = splice(lo, 1) - Zp<QT>::kMagic;
-          const float l2 = splice(lo, 2) - Zp<QT>::kMagic, l3 = splice(lo, 3) - Zp<QT>::kMagic;
-          const float h0 = splice(hi, 0) - Zp<QT>::kMagic, h1 = splice(hi, 1) - Zp<QT>::kMagic;
-          const float h2 = splice(hi, 2) - Zp<QT>::kMagic, h3 = splice(hi, 3) - Zp<QT>::kMagic;
+          float2 part[M];
+#pragma unroll
+          for (int i = 0; i < M; ++i) part[i] = make_float2(0.0f, 0.0f);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            // x pairs (2t,2t+1), (2t+8,2t+9), (2t+16,2t+17), (2t+24,2t+25) sit in float4 t/2, 2+t/2, ...
+            float2 v0, v1, v2, v3;
+            if constexpr (QT == MQ_Q8_0) {
+              const uint32_t u0 = q[r][8 * t + 2 * j] ^ 0x80808080u, u1 = q[r][8 * t + 2 * j + 1] ^ 0x80808080u;
+              v0 = decode_pair<QT>(u0, 0, 1);  // k 2t, 2t+1
+              v1 = decode_pair<QT>(u0, 2, 3);  // k 2t+8, 2t+9
+              v2 = decode_pair<QT>(u1, 0, 1);  // k 2t+16, 2t+17
+              v3 = decode_pair<QT>(u1, 2, 3);  // k 2t+24, 2t+25
+            } else {
+              const uint32_t wd = q[r][4 * t + j];
+              const uint32_t lo = wd & 0x0F0F0F0Fu, hi = (wd >> 4) & 0x0F0F0F0Fu;
+              v0 = decode_pair<QT>(lo, 0, 2);  // k 2t, 2t+1
+              v1 = decode_pair<QT>(lo, 1, 3);  // k 2t+8, 2t+9
+              v2 = decode_pair<QT>(hi, 0, 2);  // k 2t+16, 2t+17
+              v3 = decode_pair<QT>(hi, 1, 3);  // k 2t+24, 2t+25
+            }
+#pragma unroll
+            for (int i = 0; i < M; ++i) {
+              const float4 xa = xv[i][t >> 1], xb = xv[i][2 + (t >> 1)], xc = xv[i][4 + (t >> 1)],
+                           xd = xv[i][6 + (t >> 1)];
+              const bool odd = t & 1;
+              part[i] = __ffma2_rn(v0, odd ? make_float2(xa.z, xa.w) : make_float2(xa.x, xa.y), part[i]);
+              part[i] = __ffma2_rn(v1, odd ? make_float2(xb.z, xb.w) : make_float2(xb.x, xb.y), part[i]);
+              part[i] = __ffma2_rn(v2, odd ? make_float2(xc.z, xc.w) : make_float2(xc.x, xc.y), part[i]);
+              part[i] = __ffma2_rn(v3, odd ? make_float2(xd.z, xd.w) : make_float2(xd.x, xd.y), part[i]);
+            }
+          }
 #pragma unroll
           for (int i = 0; i < M; ++i) {
-            part[r][i] = dot4(l0, l1, l2, l3, xl[i], part[r][i]);
-            part[r][i] = dot4(h0, h1, h2, h3, xh[i], part[r][i]);
+            acc[r][i] = __ffma2_rn(make_float2(dsc[r][j], dsc[r][j]), part[i], acc[r][i]);
+            if constexpr (QT == MQ_Q4_1) acc[r][i].x = fmaf(msc[r][j], xs[i], acc[r][i].x);
           }
         }
       }
     }
-#pragma unroll
-    for (int r = 0; r < RPW; ++r)
-#pragma unroll
-      for (int i = 0; i < M; ++i) {
-        acc[r][i] = fmaf(dsc[r], part[r][i], acc[r][i]);
-        if constexpr (QT == MQ_Q4_1) acc[r][i] = fmaf(msc[r], xs[i], acc[r][i]);
-      }
   }
 
-  // Warp reduction, then a fixed-order combine of the warps' partials.
+  // Warp reduction, then a fixed-order combine of the K-split warps.
   __shared__ float red[8][RPW * M];
 #pragma unroll
   for (int r = 0; r < RPW; ++r)
 #pragma unroll
     for (int i = 0; i < M; ++i) {
-      float v = acc[r][i];
+      float v = acc[r][i].x + acc[r][i].y;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
       if (lane == 0) red[warp][r * M + i] = v;
     }
   __syncthreads();
-  for (int t = threadIdx.x; t < RPW * M; t += blockDim.x) {
-    const int r = t / M, i = t % M;
-    if (r >= nrow) continue;
-    float v = red[0][t];
-    for (int ww = 1; ww < nwarps; ++ww) v += red[ww][t];
-    const int n = row0 + r;
+  const int nout = warps_r * RPW * M;
+  for (int o = threadIdx.x; o < nout; o += blockDim.x) {
+    const int wr2 = o / (RPW * M), e = o % (RPW * M), r = e / M, i = e % M;
+    const int n = (blockIdx.x * warps_r + wr2) * RPW + r;
+    if (n >= w.rows) continue;
+    float v = red[wr2 * warps_k][e];
+    for (int k2 = 1; k2 < warps_k; ++k2) v += red[wr2 * warps_k + k2][e];
     if (a.bias) v += a.bias[n];
     a.y[(int64_t)i * a.ldy + n] = v;
   }

@@ -23,20 +23,22 @@ struct Planes {
 __global__ void repack_kernel(const uint8_t *__restrict__ src, int qtype, int rows, int nb, Planes p) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)rows * nb) return;
-  const int64_t r = i / nb, b = i % nb;
+  const int64_t r = i / nb;
+  const int b = (int)(i % nb);
   const int bb = block_bytes(qtype), qb = block_qbytes(qtype), hdr = bb - qb;
   const uint8_t *blk = src + i * bb;
   p.d[r * p.ld_s + b] = (uint16_t)(blk[0] | (blk[1] << 8));
   if (qtype == MQ_Q4_1) p.mn[r * p.ld_s + b] = (uint16_t)(blk[2] | (blk[3] << 8));
-  uint8_t *dst = p.qs + r * p.ld_qs + b * qb;
-  for (int j = 0; j < qb; ++j) dst[j] = blk[hdr + j];
+  uint8_t *grp = p.qs + r * p.ld_qs + (int64_t)(b >> 2) * group_bytes(qtype);
+  for (int q = 0; q < qb; ++q) grp[permuted_pos(qtype, q, b & 3)] = blk[hdr + q];
 }
 
 // Device planes -> GGUF block stream (the inverse of repack_kernel).
 __global__ void unpack_kernel(uint8_t *__restrict__ dst, int qtype, int rows, int nb, const Planes p) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)rows * nb) return;
-  const int64_t r = i / nb, b = i % nb;
+  const int64_t r = i / nb;
+  const int b = (int)(i % nb);
   const int bb = block_bytes(qtype), qb = block_qbytes(qtype), hdr = bb - qb;
   uint8_t *blk = dst + i * bb;
   const uint16_t d = p.d[r * p.ld_s + b];
@@ -47,8 +49,8 @@ __global__ void unpack_kernel(uint8_t *__restrict__ dst, int qtype, int rows, in
     blk[2] = (uint8_t)(m & 255);
     blk[3] = (uint8_t)(m >> 8);
   }
-  const uint8_t *q = p.qs + r * p.ld_qs + b * qb;
-  for (int j = 0; j < qb; ++j) blk[hdr + j] = q[j];
+  const uint8_t *grp = p.qs + r * p.ld_qs + (int64_t)(b >> 2) * group_bytes(qtype);
+  for (int q = 0; q < qb; ++q) blk[hdr + q] = grp[permuted_pos(qtype, q, b & 3)];
 }
 
 // Failure kinds of quantize_block (mapped to MQ_ERR_* and the reference's
@@ -75,6 +77,12 @@ __host__ __device__ inline int quantize_block(int qtype, const float *src, int n
     hi = hi < x ? x : hi;
     peak = fabsf(x) > fabsf(peak) ? x : peak;
   }
+  // The reference's min/max start at +0 and only a strictly smaller/larger
+  // value replaces them, so a zero result is always +0. A compiler may lower
+  // the selects above to a hardware min/max that returns -0 for (-0, +0);
+  // adding +0 canonicalises the sign (x + 0 == x for every non-zero x).
+  lo += 0.0f;
+  hi += 0.0f;
   float scale = qtype == MQ_Q8_0 ? fabsf(peak) / 127.0f : qtype == MQ_Q4_0 ? peak / -8.0f : (hi - lo) / 15.0f;
   const uint16_t sh = f32_to_f16_rne(scale);
   scale = f16_to_f32(sh);

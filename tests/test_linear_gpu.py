@@ -207,3 +207,41 @@ def test_dimension_mismatch_raises(mq, cuda_device):
     with pytest.raises(RuntimeError, match="dimension mismatch"):
         w.linear(torch.zeros(63, device=f"cuda:{cuda_device}"))
     assert "CUDA devices=" in mq.CudaDeviceInfo()
+
+
+PATHS = {1: "simt_gemv", 3: "mma_sync_gemv", 4: "tcgen05_decode", 2: "tcgen05_gemm"}
+
+
+@pytest.mark.parametrize("path", sorted(PATHS), ids=lambda p: PATHS[p])
+@pytest.mark.parametrize("q", QTYPES, ids=lambda q: NAMES[q])
+def test_every_path_against_oracle(mq, oracle, cuda_device, path, q):
+    """Each kernel, forced, on odd shapes: tail blocks (K % 32), row tails
+    (N % 16, N % 128), activation counts around every tile edge."""
+    ms = {1: [1, 2, 3], 3: [1, 5, 8, 9, 16, 17, 32, 33], 4: [1, 2, 4, 5, 16, 17, 32, 33],
+          2: [1, 7, 128, 129, 300]}[path]
+    for rows, cols in [(300, 4097), (136, 320), (1000, 96)]:
+        for m in ms:
+            s, x, y_ref, bound = _llama_case(mq, oracle, q, rows, cols, m, seed=rows * 7 + m + path)
+            assert_linear_close(gpu_linear(mq, s, x, cuda_device, path=path), y_ref, bound)
+
+
+def test_prefill_ragged_q8_0_rows_checked(mq, oracle, cuda_device):
+    """The prefill configuration (W 11008x4096 and 4096x11008, 8 requests of
+    lengths 1..512, M = 1456) through the tcgen05 GEMM; 192 output rows spread
+    over the matrix are checked against the oracle (rows are independent)."""
+    torch = _torch()
+    lengths = [1, 7, 33, 64, 128, 200, 511, 512]
+    m = sum(lengths)
+    rng = np.random.default_rng(1456)
+    for rows, cols in [(11008, 4096), (4096, 11008)]:
+        w = (rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02))
+        s = mq.QuantizeTensor(w, Q8_0)
+        x = rng.standard_normal((m, cols), dtype=np.float32)
+        y = gpu_linear(mq, s, x, cuda_device, path=0)
+        pick = np.sort(rng.choice(rows, 192, replace=False))
+        bb = ((cols + 31) // 32) * 34
+        sub = np.concatenate([s.bytes[r * bb:(r + 1) * bb] for r in pick])
+        y_ref = oracle.linear(Q8_0, sub, len(pick), cols, x, threads=THREADS)
+        bound = abs_dot_bound(oracle.dequantize(Q8_0, sub, len(pick), cols), x)
+        assert_linear_close(y[:, pick], y_ref, bound)
+        torch.cuda.synchronize()
