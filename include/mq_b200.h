@@ -127,6 +127,22 @@ int mq_linear(const mq_weight *w, const float *x, int m, int ldx, const float *b
 int mq_linear_ragged(const mq_weight *w, const float *x, const int *offsets, int n_seqs, int ldx,
                      const float *bias, float *y, int ldy, void *stream);
 
+/* Same product as mq_linear for decode-sized batches, for callers that cannot
+ * allocate device memory: they own every device byte through their own pool,
+ * run under a fixed memory budget, or call from a hot loop where cudaMalloc's
+ * device-wide synchronisation and latency are not acceptable. It has no
+ * counterpart in the reference. This call allocates nothing: its scratch is a
+ * fixed 3.1 MiB device array that every GPU loading the library holds until
+ * the process exits. Limits: 1 <= m <= 16 (m == 0 is a no-op), weight cols
+ * <= 16384 and rows <= 131072; larger requests fail with MQ_ERR_INVALID. The
+ * first call on a device resolves the array's device address there, so make
+ * that first call before any stream capture. All calls on a device share the
+ * array, so calls that overlap on the GPU (other streams, other host threads)
+ * race and must be serialised by the caller. A bounded device wait that runs
+ * out writes NaN to the outputs. */
+int mq_linear_noalloc(const mq_weight *w, const float *x, int m, int ldx, const float *bias, float *y, int ldy,
+                      void *stream);
+
 /* Kernel selection for the next mq_linear calls on this thread:
  * 0 = automatic (default): SIMT GEMV for m == 1, tcgen05 decode GEMM for
  *     m <= 32, tcgen05 prefill GEMM above;

@@ -37,6 +37,7 @@ SIGNATURES = {
     "mq_weight_export": (_i, [_vp, _vp, _sz]),
     "mq_linear": (_i, [_vp, _vp, _i, _i, _vp, _vp, _i, _vp]),
     "mq_linear_ragged": (_i, [_vp, _vp, C.POINTER(_i), _i, _i, _vp, _vp, _i, _vp]),
+    "mq_linear_noalloc": (_i, [_vp, _vp, _i, _i, _vp, _vp, _i, _vp]),
     "mq_set_path": (_i, [_i]),
     "mq_kernel_launches": (C.c_uint64, []),
     "mq_device_info": (_i, [C.c_char_p, _sz]),

@@ -268,6 +268,55 @@ int run_tcgemv(const mq_weight *wt, const float *x, int m, int64_t ldx, const fl
   return MQ_OK;
 }
 
+DecPlan tcdec_plan(const WeightView &w, int device) {
+  DecPlan p;
+  const bool q8 = w.qtype == MQ_Q8_0;
+  const int blocks_per_step = q8 ? 4 : 8;
+  p.steps_total = q8 ? w.nb4 : (w.nb4 + 1) / 2;
+  p.kpad = p.steps_total * blocks_per_step * 32;
+  p.tiles = (w.rows_pad + kDecRows - 1) / kDecRows;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  int ksplit = env_threshold("MQ_TCDEC_KSPLIT", 0);
+  if (ksplit <= 0) ksplit = std::max(1, sms / p.tiles);  // one wave of one CTA per SM
+  p.ksplit = std::max(1, std::min(ksplit, p.steps_total));
+  return p;
+}
+
+int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const float *bias, float *y, int64_t ldy,
+                 cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort) {
+  const int bn = mm <= 16 ? 16 : 32;
+  dec_prep_kernel<<<bn, 1024, 0, s>>>(x, ldx, mm, w.cols, plan.kpad, bn, buf.xh, buf.xl, buf.xsum, buf.xinv,
+                                      w.qtype == MQ_Q4_1);
+  count_launch();
+  MQ_CUDA(cudaGetLastError());
+  CUtensorMap tq, th, tl;
+  int rc;
+  if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.qs, w.rows_pad, w.ld_qs, w.ld_qs, 128, kDecRows)))
+    return rc;
+  if ((rc = make_tmap(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf.xh, bn, plan.kpad, plan.kpad, 64, bn))) return rc;
+  if ((rc = make_tmap(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf.xl, bn, plan.kpad, plan.kpad, 64, bn))) return rc;
+  DecArgs a{w, mm, buf.xinv, buf.xsum, bias, y, ldy, buf.partial, buf.tickets, plan.ksplit, plan.steps_total,
+            buf.err, nan_on_abort};
+  cudaError_t e;
+  switch (w.qtype) {
+  case MQ_Q8_0:
+    e = bn == 16 ? launch_tcdec_t<MQ_Q8_0, 16, 3, 4>(tq, th, tl, a, plan.tiles, s)
+                 : launch_tcdec_t<MQ_Q8_0, 32, 3, 4>(tq, th, tl, a, plan.tiles, s);
+    break;
+  case MQ_Q4_0:
+    e = bn == 16 ? launch_tcdec_t<MQ_Q4_0, 16, 4, 4>(tq, th, tl, a, plan.tiles, s)
+                 : launch_tcdec_t<MQ_Q4_0, 32, 4, 4>(tq, th, tl, a, plan.tiles, s);
+    break;
+  default:
+    e = bn == 16 ? launch_tcdec_t<MQ_Q4_1, 16, 4, 4>(tq, th, tl, a, plan.tiles, s)
+                 : launch_tcdec_t<MQ_Q4_1, 32, 4, 4>(tq, th, tl, a, plan.tiles, s);
+    break;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "tcgen05 decode launch");
+  return MQ_OK;
+}
+
 // tcgen05 decode GEMM: up to 32 activation rows per launch (split + kernel).
 int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
               cudaStream_t s) {
@@ -279,58 +328,28 @@ int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
     return fail(MQ_ERR_TIMEOUT, "an earlier tensor-core launch on device %d ran out of a bounded wait", wt->device);
   }
   const WeightView &w = wt->v;
-  const bool q8 = w.qtype == MQ_Q8_0;
-  const int blocks_per_step = q8 ? 4 : 8;
-  const int steps_total = q8 ? w.nb4 : (w.nb4 + 1) / 2;
-  const int kpad = steps_total * blocks_per_step * 32;
-  const int tiles = (w.rows_pad + kDecRows - 1) / kDecRows;
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, wt->device);
-  int ksplit = env_threshold("MQ_TCDEC_KSPLIT", 0);
-  if (ksplit <= 0) ksplit = std::max(1, sms / tiles);  // one wave of one CTA per SM
-  ksplit = std::max(1, std::min(ksplit, steps_total));
+  const DecPlan plan = tcdec_plan(w, wt->device);
   int *tickets = nullptr;
-  if ((rc = tickets_for(wt->device, s, (size_t)tiles, &tickets))) return rc;
+  if ((rc = tickets_for(wt->device, s, (size_t)plan.tiles, &tickets))) return rc;
   for (int i0 = 0; i0 < m; i0 += 32) {
     const int mm = std::min(32, m - i0);
     const int bn = mm <= 16 ? 16 : 32;
-    const size_t xbytes = (size_t)bn * kpad * 2;
-    const size_t sbytes = (size_t)(kpad / 32) * bn * 4;
-    const size_t pbytes = ksplit > 1 ? (size_t)ksplit * tiles * kDecRows * bn * 4 : 0;
+    const size_t xbytes = (size_t)bn * plan.kpad * 2;
+    const size_t sbytes = (size_t)(plan.kpad / 32) * bn * 4;
+    const size_t pbytes = plan.ksplit > 1 ? (size_t)plan.ksplit * plan.tiles * kDecRows * bn * 4 : 0;
     void *ws = nullptr;
     if ((rc = workspace_for(wt->device, s, 2 * xbytes + sbytes + 256 + pbytes + 1024, &ws))) return rc;
     uint8_t *base = static_cast<uint8_t *>(ws);
-    __half *xh = reinterpret_cast<__half *>(base);
-    __half *xl = reinterpret_cast<__half *>(base + xbytes);
-    float *xsum = reinterpret_cast<float *>(base + 2 * xbytes);
-    float *xinv = reinterpret_cast<float *>(base + 2 * xbytes + sbytes);
-    float *partial = reinterpret_cast<float *>(base + ((2 * xbytes + sbytes + 256 + 1023) & ~size_t(1023)));
-    dec_prep_kernel<<<bn, 1024, 0, s>>>(x + (int64_t)i0 * ldx, ldx, mm, w.cols, kpad, bn, xh, xl, xsum, xinv,
-                                        w.qtype == MQ_Q4_1);
-    count_launch();
-    MQ_CUDA(cudaGetLastError());
-    CUtensorMap tq, th, tl;
-    if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.qs, w.rows_pad, w.ld_qs, w.ld_qs, 128, kDecRows)))
+    DecBuffers buf;
+    buf.xh = reinterpret_cast<__half *>(base);
+    buf.xl = reinterpret_cast<__half *>(base + xbytes);
+    buf.xsum = reinterpret_cast<float *>(base + 2 * xbytes);
+    buf.xinv = reinterpret_cast<float *>(base + 2 * xbytes + sbytes);
+    buf.partial = reinterpret_cast<float *>(base + ((2 * xbytes + sbytes + 256 + 1023) & ~size_t(1023)));
+    buf.tickets = tickets;
+    buf.err = err_dev;
+    if ((rc = tcdec_launch(w, x + (int64_t)i0 * ldx, mm, ldx, bias, y + (int64_t)i0 * ldy, ldy, s, plan, buf, 0)))
       return rc;
-    if ((rc = make_tmap(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, bn, kpad, kpad, 64, bn))) return rc;
-    if ((rc = make_tmap(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xl, bn, kpad, kpad, 64, bn))) return rc;
-    DecArgs a{w, mm, xinv, xsum, bias, y + (int64_t)i0 * ldy, ldy, partial, tickets, ksplit, steps_total, err_dev};
-    cudaError_t e;
-    switch (w.qtype) {
-    case MQ_Q8_0:
-      e = bn == 16 ? launch_tcdec_t<MQ_Q8_0, 16, 3, 4>(tq, th, tl, a, tiles, s)
-                   : launch_tcdec_t<MQ_Q8_0, 32, 3, 4>(tq, th, tl, a, tiles, s);
-      break;
-    case MQ_Q4_0:
-      e = bn == 16 ? launch_tcdec_t<MQ_Q4_0, 16, 4, 4>(tq, th, tl, a, tiles, s)
-                   : launch_tcdec_t<MQ_Q4_0, 32, 4, 4>(tq, th, tl, a, tiles, s);
-      break;
-    default:
-      e = bn == 16 ? launch_tcdec_t<MQ_Q4_1, 16, 4, 4>(tq, th, tl, a, tiles, s)
-                   : launch_tcdec_t<MQ_Q4_1, 32, 4, 4>(tq, th, tl, a, tiles, s);
-      break;
-    }
-    if (e != cudaSuccess) return cuda_fail(e, "tcgen05 decode launch");
   }
   return MQ_OK;
 }

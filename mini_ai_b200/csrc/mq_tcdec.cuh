@@ -34,6 +34,7 @@
 
 #include "mq_common.cuh"
 #include "mq_sm100.cuh"
+#include "mq_tcdec_api.h"
 
 namespace mq {
 
@@ -56,6 +57,7 @@ struct DecArgs {
   int ksplit;
   int steps_total;       // packed steps over the whole K
   int *err;
+  int nan_on_abort;      // on a timed-out wait, write NaN outputs instead of skipping them
 };
 
 template <int QT> struct DecQ {
@@ -367,7 +369,12 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       }
     }
     // ------------------------------------------------ epilogue
-    const bool ok = !*abort;
+    const bool aborted = *abort;
+    if (aborted && a.nan_on_abort) {
+#pragma unroll
+      for (int c = 0; c < BN; ++c) acc[c] = __int_as_float(0x7fc00000);
+    }
+    const bool ok = !aborted || a.nan_on_abort;
     if (a.ksplit == 1) {
       if (ok && row_ok) {
         const float bias = a.bias ? a.bias[n] : 0.0f;

@@ -1,0 +1,38 @@
+// Host interface of the tcgen05 decode GEMM, shared by mq_linear (scratch from
+// the per-stream workspace) and mq_linear_noalloc (scratch in a static device
+// array). Definitions live in mq_gemm_host.cuh.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "mq_common.cuh"
+
+namespace mq {
+
+// Packed steps, padded K, 128-row tiles and the split-K factor of a weight.
+struct DecPlan {
+  int steps_total, kpad, tiles, ksplit;
+};
+
+// Scratch one launch pair needs.
+struct DecBuffers {
+  __half *xh, *xl;    // [bn][kpad] each: activation rows split into fp16 hi + lo
+  float *xsum;        // [kpad / 32][bn]: scaled block sums of x (Q4_1)
+  float *xinv;        // [bn]: 2^-e per activation row
+  float *partial;     // [ksplit][tiles * 128][bn] when ksplit > 1
+  int *tickets;       // [tiles], zero between launches
+  int *err;           // device-visible timeout flag
+};
+
+DecPlan tcdec_plan(const WeightView &w, int device);
+
+// One launch pair (activation split + decode GEMM) for m <= 32 rows; bn is 16
+// for m <= 16, else 32. nan_on_abort: a timed-out bounded wait writes NaN to
+// the outputs instead of leaving them unwritten.
+int tcdec_launch(const WeightView &w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
+                 cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort);
+
+bool gemm_supported(int device);
+
+}  // namespace mq
