@@ -132,7 +132,7 @@ int mq_linear_ragged(const mq_weight *w, const float *x, const int *offsets, int
  * run under a fixed memory budget, or call from a hot loop where cudaMalloc's
  * device-wide synchronisation and latency are not acceptable. It has no
  * counterpart in the reference. This call allocates nothing: its scratch is a
- * fixed 3.1 MiB device array that every GPU loading the library holds until
+ * fixed 3.6 MiB device array that every GPU loading the library holds until
  * the process exits. Limits: 1 <= m <= 16 (m == 0 is a no-op), weight cols
  * <= 16384 and rows <= 131072; larger requests fail with MQ_ERR_INVALID. The
  * first call on a device resolves the array's device address there, so make

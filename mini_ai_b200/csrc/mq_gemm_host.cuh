@@ -128,7 +128,8 @@ int make_tmap_bf16(CUtensorMap *map, const void *base, int rows, int cols, int b
 // elements: dims {cols, rows}, box {box_cols, box_rows}; out-of-range reads
 // return zeros.
 int make_tmap(CUtensorMap *map, CUtensorMapDataType dtype, int elem, const void *base, int64_t rows, int64_t cols,
-              int64_t row_stride_elems, int box_cols, int box_rows) {
+              int64_t row_stride_elems, int box_cols, int box_rows,
+              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   int rc = encode_fn(&enc);
   if (rc) return rc;
@@ -137,26 +138,32 @@ int make_tmap(CUtensorMap *map, CUtensorMapDataType dtype, int elem, const void 
   const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = enc(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                         swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(MQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return MQ_OK;
 }
 
-template <int QT, int BN, int PS, int AS>
-cudaError_t launch_tcdec_t(const CUtensorMap &tq, const CUtensorMap &th, const CUtensorMap &tl, const DecArgs &a,
-                           int tiles, cudaStream_t s) {
-  using L = DecSmem<QT, BN, PS, AS>;
+template <int QT, int BN, int NC>
+cudaError_t launch_tcdec_t(const CUtensorMap &tq, const CUtensorMap &td, const CUtensorMap &tm, const CUtensorMap &th,
+                           const CUtensorMap &tl, const DecArgs &a, int grid, cudaStream_t s) {
+  using L = DecCfg<QT, BN>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e =
-        cudaFuncSetAttribute(tcdec_kernel<QT, BN, PS, AS>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    cudaError_t e = cudaFuncSetAttribute(tcdec_kernel<QT, BN, NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  tcdec_kernel<QT, BN, PS, AS><<<dim3(tiles, a.ksplit), kDecThreads, L::kAlloc, s>>>(tq, th, tl, a);
+  tcdec_kernel<QT, BN, NC><<<grid, kDecThreads, L::kAlloc, s>>>(tq, td, tm, th, tl, a);
   count_launch();
   return cudaGetLastError();
+}
+
+template <int QT>
+cudaError_t launch_tcdec_q(const CUtensorMap &tq, const CUtensorMap &td, const CUtensorMap &tm, const CUtensorMap &th,
+                           const CUtensorMap &tl, const DecArgs &a, int grid, int m, cudaStream_t s) {
+  if (m <= 4) return launch_tcdec_t<QT, 16, 4>(tq, td, tm, th, tl, a, grid, s);
+  if (m <= 16) return launch_tcdec_t<QT, 16, 16>(tq, td, tm, th, tl, a, grid, s);
+  return launch_tcdec_t<QT, 32, 32>(tq, td, tm, th, tl, a, grid, s);
 }
 
 template <int QT, int BN, int STAGES>
@@ -268,18 +275,17 @@ int run_tcgemv(const mq_weight *wt, const float *x, int m, int64_t ldx, const fl
   return MQ_OK;
 }
 
-DecPlan tcdec_plan(const WeightView &w, int device) {
+DecPlan tcdec_plan(const WeightView &w, int device, int max_grid) {
   DecPlan p;
-  const bool q8 = w.qtype == MQ_Q8_0;
-  const int blocks_per_step = q8 ? 4 : 8;
-  p.steps_total = q8 ? w.nb4 : (w.nb4 + 1) / 2;
-  p.kpad = p.steps_total * blocks_per_step * 32;
+  p.steps = (w.nb4 + 1) / 2;  // 8 blocks (two 4-block groups) per packed step
+  p.kpad = p.steps * kDecBlocksPerStep * 32;
   p.tiles = (w.rows_pad + kDecRows - 1) / kDecRows;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  int ksplit = env_threshold("MQ_TCDEC_KSPLIT", 0);
-  if (ksplit <= 0) ksplit = std::max(1, sms / p.tiles);  // one wave of one CTA per SM
-  p.ksplit = std::max(1, std::min(ksplit, p.steps_total));
+  int grid = env_threshold("MQ_TCDEC_GRID", 0);
+  if (grid <= 0) grid = sms;
+  if (max_grid > 0) grid = std::min(grid, max_grid);
+  p.grid = std::max(1, std::min(grid, p.tiles * p.steps));
   return p;
 }
 
@@ -290,28 +296,25 @@ int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const
                                       w.qtype == MQ_Q4_1);
   count_launch();
   MQ_CUDA(cudaGetLastError());
-  CUtensorMap tq, th, tl;
+  CUtensorMap tq, td, tm, th, tl;
   int rc;
   if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.qs, w.rows_pad, w.ld_qs, w.ld_qs, 128, kDecRows)))
     return rc;
+  if ((rc = make_tmap(&td, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.d, w.rows_pad, w.ld_s, w.ld_s, kDecBlocksPerStep,
+                      kDecRows, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  if ((rc = make_tmap(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.qtype == MQ_Q4_1 ? w.mn : w.d, w.rows_pad, w.ld_s,
+                      w.ld_s, kDecBlocksPerStep, kDecRows, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
   if ((rc = make_tmap(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf.xh, bn, plan.kpad, plan.kpad, 64, bn))) return rc;
   if ((rc = make_tmap(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf.xl, bn, plan.kpad, plan.kpad, 64, bn))) return rc;
-  DecArgs a{w, mm, buf.xinv, buf.xsum, bias, y, ldy, buf.partial, buf.tickets, plan.ksplit, plan.steps_total,
-            buf.err, nan_on_abort};
+  DecArgs a{w, mm, buf.xinv, buf.xsum, bias, y, ldy, buf.partial, buf.tickets, plan.steps, plan.tiles, buf.err,
+            nan_on_abort};
   cudaError_t e;
   switch (w.qtype) {
-  case MQ_Q8_0:
-    e = bn == 16 ? launch_tcdec_t<MQ_Q8_0, 16, 3, 4>(tq, th, tl, a, plan.tiles, s)
-                 : launch_tcdec_t<MQ_Q8_0, 32, 3, 4>(tq, th, tl, a, plan.tiles, s);
-    break;
-  case MQ_Q4_0:
-    e = bn == 16 ? launch_tcdec_t<MQ_Q4_0, 16, 4, 4>(tq, th, tl, a, plan.tiles, s)
-                 : launch_tcdec_t<MQ_Q4_0, 32, 4, 4>(tq, th, tl, a, plan.tiles, s);
-    break;
-  default:
-    e = bn == 16 ? launch_tcdec_t<MQ_Q4_1, 16, 4, 4>(tq, th, tl, a, plan.tiles, s)
-                 : launch_tcdec_t<MQ_Q4_1, 32, 4, 4>(tq, th, tl, a, plan.tiles, s);
-    break;
+  case MQ_Q8_0: e = launch_tcdec_q<MQ_Q8_0>(tq, td, tm, th, tl, a, plan.grid, mm, s); break;
+  case MQ_Q4_0: e = launch_tcdec_q<MQ_Q4_0>(tq, td, tm, th, tl, a, plan.grid, mm, s); break;
+  default: e = launch_tcdec_q<MQ_Q4_1>(tq, td, tm, th, tl, a, plan.grid, mm, s); break;
   }
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 decode launch");
   return MQ_OK;
@@ -336,7 +339,7 @@ int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
     const int bn = mm <= 16 ? 16 : 32;
     const size_t xbytes = (size_t)bn * plan.kpad * 2;
     const size_t sbytes = (size_t)(plan.kpad / 32) * bn * 4;
-    const size_t pbytes = plan.ksplit > 1 ? (size_t)plan.ksplit * plan.tiles * kDecRows * bn * 4 : 0;
+    const size_t pbytes = (size_t)plan.grid * 2 * kDecRows * bn * 4;
     void *ws = nullptr;
     if ((rc = workspace_for(wt->device, s, 2 * xbytes + sbytes + 256 + pbytes + 1024, &ws))) return rc;
     uint8_t *base = static_cast<uint8_t *>(ws);

@@ -20,13 +20,13 @@ namespace {
 constexpr int kNaMaxM = 16;           // activation rows per call
 constexpr int kNaMaxKpad = 16384;     // padded K: weights with cols <= 16384
 constexpr int kNaMaxTiles = 1024;     // 128-row tiles: weights with rows <= 131072
-constexpr int kNaMaxSplitCtas = 256;  // split-K partial slots (tiles x splits)
+constexpr int kNaMaxGrid = 160;       // persistent CTAs (two partial tiles each)
 constexpr int kNaMaxDevices = 64;
 
 constexpr size_t kNaX = (size_t)kNaMaxM * kNaMaxKpad * sizeof(__half);        // 512 KiB, hi and lo each
 constexpr size_t kNaSum = (size_t)(kNaMaxKpad / 32) * kNaMaxM * sizeof(float);  // 32 KiB
 constexpr size_t kNaInv = 256;
-constexpr size_t kNaPart = (size_t)kNaMaxSplitCtas * 128 * kNaMaxM * sizeof(float);  // 2 MiB
+constexpr size_t kNaPart = (size_t)kNaMaxGrid * 2 * 128 * kNaMaxM * sizeof(float);  // 2.5 MiB
 constexpr size_t kNaTickets = (size_t)kNaMaxTiles * sizeof(int);
 constexpr size_t kNaErr = 256;
 
@@ -37,7 +37,7 @@ constexpr size_t kOffInv = kOffSum + kNaSum;
 constexpr size_t kOffPart = kOffInv + kNaInv;
 constexpr size_t kOffTickets = kOffPart + kNaPart;
 constexpr size_t kOffErr = kOffTickets + kNaTickets;
-constexpr size_t kNaBytes = kOffErr + kNaErr;  // 3.1 MiB
+constexpr size_t kNaBytes = kOffErr + kNaErr;  // 3.6 MiB
 
 }  // namespace
 
@@ -99,15 +99,13 @@ extern "C" int mq_linear_noalloc(const mq_weight *w, const float *x, int m, int 
   if (g.err != cudaSuccess) return cuda_fail(g.err, "cudaSetDevice");
   if (!gemm_supported(w->device))
     return fail(MQ_ERR_UNSUPPORTED, "mq_linear_noalloc needs an sm_100 device (device %d)", w->device);
-  DecPlan plan = tcdec_plan(w->v, w->device);
+  const DecPlan plan = tcdec_plan(w->v, w->device, kNaMaxGrid);
   if (plan.kpad > kNaMaxKpad)
     return fail(MQ_ERR_INVALID, "mq_linear_noalloc: weight has %d columns; the static scratch holds at most %d",
                 w->v.cols, kNaMaxKpad);
   if (plan.tiles > kNaMaxTiles)
     return fail(MQ_ERR_INVALID, "mq_linear_noalloc: weight has %d rows; the static scratch holds at most %d",
                 w->v.rows, kNaMaxTiles * 128);
-  if (plan.ksplit > 1 && plan.ksplit * plan.tiles > kNaMaxSplitCtas)
-    plan.ksplit = std::max(1, kNaMaxSplitCtas / plan.tiles);
   uint8_t *base = nullptr;
   int rc = na_scratch(w->device, &base);
   if (rc) return rc;

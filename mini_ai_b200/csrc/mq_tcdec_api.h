@@ -10,9 +10,10 @@
 
 namespace mq {
 
-// Packed steps, padded K, 128-row tiles and the split-K factor of a weight.
+// Packed K steps per tile, padded K, 128-row tiles and the persistent grid
+// (one CTA per SM, at most one per step of work).
 struct DecPlan {
-  int steps_total, kpad, tiles, ksplit;
+  int steps, kpad, tiles, grid;
 };
 
 // Scratch one launch pair needs.
@@ -20,12 +21,13 @@ struct DecBuffers {
   __half *xh, *xl;    // [bn][kpad] each: activation rows split into fp16 hi + lo
   float *xsum;        // [kpad / 32][bn]: scaled block sums of x (Q4_1)
   float *xinv;        // [bn]: 2^-e per activation row
-  float *partial;     // [ksplit][tiles * 128][bn] when ksplit > 1
+  float *partial;     // [grid][2][128][bn]: head / tail partial tile of every CTA
   int *tickets;       // [tiles], zero between launches
   int *err;           // device-visible timeout flag
 };
 
-DecPlan tcdec_plan(const WeightView &w, int device);
+// max_grid caps the persistent grid (0: one CTA per SM).
+DecPlan tcdec_plan(const WeightView &w, int device, int max_grid = 0);
 
 // One launch pair (activation split + decode GEMM) for m <= 32 rows; bn is 16
 // for m <= 16, else 32. nan_on_abort: a timed-out bounded wait writes NaN to
