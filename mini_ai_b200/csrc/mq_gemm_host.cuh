@@ -144,8 +144,8 @@ int make_tmap(CUtensorMap *map, CUtensorMapDataType dtype, int elem, const void 
 }
 
 template <int QT, int BN, int NC>
-cudaError_t launch_tcdec_t(const CUtensorMap &tq, const CUtensorMap &td, const CUtensorMap &tm, const CUtensorMap &th,
-                           const CUtensorMap &tl, const DecArgs &a, int grid, cudaStream_t s) {
+cudaError_t launch_tcdec_t(const CUtensorMap &tq, const CUtensorMap &td, const CUtensorMap &tm, const CUtensorMap &tx,
+                           const DecArgs &a, int grid, cudaStream_t s) {
   using L = DecCfg<QT, BN>;
   static bool configured = false;
   if (!configured) {
@@ -153,17 +153,18 @@ cudaError_t launch_tcdec_t(const CUtensorMap &tq, const CUtensorMap &td, const C
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  tcdec_kernel<QT, BN, NC><<<grid, kDecThreads, L::kAlloc, s>>>(tq, td, tm, th, tl, a);
+  tcdec_kernel<QT, BN, NC><<<grid, kDecThreads, L::kAlloc, s>>>(tq, td, tm, tx, a);
   count_launch();
   return cudaGetLastError();
 }
 
 template <int QT>
-cudaError_t launch_tcdec_q(const CUtensorMap &tq, const CUtensorMap &td, const CUtensorMap &tm, const CUtensorMap &th,
-                           const CUtensorMap &tl, const DecArgs &a, int grid, int m, cudaStream_t s) {
-  if (m <= 4) return launch_tcdec_t<QT, 16, 4>(tq, td, tm, th, tl, a, grid, s);
-  if (m <= 16) return launch_tcdec_t<QT, 16, 16>(tq, td, tm, th, tl, a, grid, s);
-  return launch_tcdec_t<QT, 32, 32>(tq, td, tm, th, tl, a, grid, s);
+cudaError_t launch_tcdec_q(const CUtensorMap &tq, const CUtensorMap &td, const CUtensorMap &tm, const CUtensorMap &tx,
+                           const DecArgs &a, int grid, int m, cudaStream_t s) {
+  if (m <= 4) return launch_tcdec_t<QT, 8, 4>(tq, td, tm, tx, a, grid, s);
+  if (m <= 8) return launch_tcdec_t<QT, 8, 8>(tq, td, tm, tx, a, grid, s);
+  if (m <= 16) return launch_tcdec_t<QT, 16, 16>(tq, td, tm, tx, a, grid, s);
+  return launch_tcdec_t<QT, 32, 32>(tq, td, tm, tx, a, grid, s);
 }
 
 template <int QT, int BN, int STAGES>
@@ -291,12 +292,12 @@ DecPlan tcdec_plan(const WeightView &w, int device, int max_grid) {
 
 int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const float *bias, float *y, int64_t ldy,
                  cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort) {
-  const int bn = mm <= 16 ? 16 : 32;
-  dec_prep_kernel<<<bn, 1024, 0, s>>>(x, ldx, mm, w.cols, plan.kpad, bn, buf.xh, buf.xl, buf.xsum, buf.xinv,
+  const int bn = dec_tile_rows(mm);
+  dec_prep_kernel<<<bn, 1024, 0, s>>>(x, ldx, mm, w.cols, plan.kpad, bn, buf.x2, buf.xsum, buf.xinv,
                                       w.qtype == MQ_Q4_1);
   count_launch();
   MQ_CUDA(cudaGetLastError());
-  CUtensorMap tq, td, tm, th, tl;
+  CUtensorMap tq, td, tm, tx;
   int rc;
   if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.qs, w.rows_pad, w.ld_qs, w.ld_qs, 128, kDecRows)))
     return rc;
@@ -306,15 +307,15 @@ int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const
   if ((rc = make_tmap(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.qtype == MQ_Q4_1 ? w.mn : w.d, w.rows_pad, w.ld_s,
                       w.ld_s, kDecBlocksPerStep, kDecRows, CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
-  if ((rc = make_tmap(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf.xh, bn, plan.kpad, plan.kpad, 64, bn))) return rc;
-  if ((rc = make_tmap(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf.xl, bn, plan.kpad, plan.kpad, 64, bn))) return rc;
+  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf.x2, 2 * bn, plan.kpad, plan.kpad, 64, 2 * bn)))
+    return rc;
   DecArgs a{w, mm, buf.xinv, buf.xsum, bias, y, ldy, buf.partial, buf.tickets, plan.steps, plan.tiles, buf.err,
             nan_on_abort};
   cudaError_t e;
   switch (w.qtype) {
-  case MQ_Q8_0: e = launch_tcdec_q<MQ_Q8_0>(tq, td, tm, th, tl, a, plan.grid, mm, s); break;
-  case MQ_Q4_0: e = launch_tcdec_q<MQ_Q4_0>(tq, td, tm, th, tl, a, plan.grid, mm, s); break;
-  default: e = launch_tcdec_q<MQ_Q4_1>(tq, td, tm, th, tl, a, plan.grid, mm, s); break;
+  case MQ_Q8_0: e = launch_tcdec_q<MQ_Q8_0>(tq, td, tm, tx, a, plan.grid, mm, s); break;
+  case MQ_Q4_0: e = launch_tcdec_q<MQ_Q4_0>(tq, td, tm, tx, a, plan.grid, mm, s); break;
+  default: e = launch_tcdec_q<MQ_Q4_1>(tq, td, tm, tx, a, plan.grid, mm, s); break;
   }
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 decode launch");
   return MQ_OK;
@@ -336,19 +337,18 @@ int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
   if ((rc = tickets_for(wt->device, s, (size_t)plan.tiles, &tickets))) return rc;
   for (int i0 = 0; i0 < m; i0 += 32) {
     const int mm = std::min(32, m - i0);
-    const int bn = mm <= 16 ? 16 : 32;
-    const size_t xbytes = (size_t)bn * plan.kpad * 2;
+    const int bn = dec_tile_rows(mm);
+    const size_t xbytes = (size_t)2 * bn * plan.kpad * 2;
     const size_t sbytes = (size_t)(plan.kpad / 32) * bn * 4;
     const size_t pbytes = (size_t)plan.grid * 2 * kDecRows * bn * 4;
     void *ws = nullptr;
-    if ((rc = workspace_for(wt->device, s, 2 * xbytes + sbytes + 256 + pbytes + 1024, &ws))) return rc;
+    if ((rc = workspace_for(wt->device, s, xbytes + sbytes + 256 + pbytes + 1024, &ws))) return rc;
     uint8_t *base = static_cast<uint8_t *>(ws);
     DecBuffers buf;
-    buf.xh = reinterpret_cast<__half *>(base);
-    buf.xl = reinterpret_cast<__half *>(base + xbytes);
-    buf.xsum = reinterpret_cast<float *>(base + 2 * xbytes);
-    buf.xinv = reinterpret_cast<float *>(base + 2 * xbytes + sbytes);
-    buf.partial = reinterpret_cast<float *>(base + ((2 * xbytes + sbytes + 256 + 1023) & ~size_t(1023)));
+    buf.x2 = reinterpret_cast<__half *>(base);
+    buf.xsum = reinterpret_cast<float *>(base + xbytes);
+    buf.xinv = reinterpret_cast<float *>(base + xbytes + sbytes);
+    buf.partial = reinterpret_cast<float *>(base + ((xbytes + sbytes + 256 + 1023) & ~size_t(1023)));
     buf.tickets = tickets;
     buf.err = err_dev;
     if ((rc = tcdec_launch(w, x + (int64_t)i0 * ldx, mm, ldx, bias, y + (int64_t)i0 * ldy, ldy, s, plan, buf, 0)))

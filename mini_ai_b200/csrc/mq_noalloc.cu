@@ -23,16 +23,15 @@ constexpr int kNaMaxTiles = 1024;     // 128-row tiles: weights with rows <= 131
 constexpr int kNaMaxGrid = 160;       // persistent CTAs (two partial tiles each)
 constexpr int kNaMaxDevices = 64;
 
-constexpr size_t kNaX = (size_t)kNaMaxM * kNaMaxKpad * sizeof(__half);        // 512 KiB, hi and lo each
+constexpr size_t kNaX = (size_t)2 * kNaMaxM * kNaMaxKpad * sizeof(__half);    // 1 MiB: hi rows, lo rows
 constexpr size_t kNaSum = (size_t)(kNaMaxKpad / 32) * kNaMaxM * sizeof(float);  // 32 KiB
 constexpr size_t kNaInv = 256;
 constexpr size_t kNaPart = (size_t)kNaMaxGrid * 2 * 128 * kNaMaxM * sizeof(float);  // 2.5 MiB
 constexpr size_t kNaTickets = (size_t)kNaMaxTiles * sizeof(int);
 constexpr size_t kNaErr = 256;
 
-constexpr size_t kOffXh = 0;
-constexpr size_t kOffXl = kOffXh + kNaX;
-constexpr size_t kOffSum = kOffXl + kNaX;
+constexpr size_t kOffX = 0;
+constexpr size_t kOffSum = kOffX + kNaX;
 constexpr size_t kOffInv = kOffSum + kNaSum;
 constexpr size_t kOffPart = kOffInv + kNaInv;
 constexpr size_t kOffTickets = kOffPart + kNaPart;
@@ -111,8 +110,7 @@ extern "C" int mq_linear_noalloc(const mq_weight *w, const float *x, int m, int 
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   DecBuffers buf;
-  buf.xh = reinterpret_cast<__half *>(base + kOffXh);
-  buf.xl = reinterpret_cast<__half *>(base + kOffXl);
+  buf.x2 = reinterpret_cast<__half *>(base + kOffX);
   buf.xsum = reinterpret_cast<float *>(base + kOffSum);
   buf.xinv = reinterpret_cast<float *>(base + kOffInv);
   buf.partial = reinterpret_cast<float *>(base + kOffPart);

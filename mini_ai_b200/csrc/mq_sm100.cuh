@@ -57,6 +57,39 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
   }
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete is
+// suspended (it issues nothing) until the phase completes or about hint_ns
+// have passed.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait for roles off the critical issue path: between polls the thread
+// sleeps in the barrier instead of spinning, so that it takes no issue slots
+// from the warps that do the work. Same bound and abort protocol.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, int *err, volatile int *abort,
+                                                uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+    if (abort && *abort) return false;
+    if (globaltimer_ns() - t0 > limit_ns) {
+      if (abort) *abort = 1;
+      if (err) atomicExch(err, 1);
+      return false;
+    }
+  }
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }

@@ -8,33 +8,59 @@
 // Exactness scheme. The A operand holds the exact integers q - zp (fp16), not
 // the scaled weights, so no rounding or range issue is introduced by the
 // per-block fp16 scale; the activation rows are scaled by a power of two and
-// split into fp16 hi + lo (22 significant bits). Each 32-weight block's MMAs
-// (two K=16 steps x hi/lo) accumulate into their own TMEM slot, and drainer
-// warps apply the block scale in fp32:  acc += d_b * D_b (+ m_b * sum_b x).
+// split into fp16 hi + lo (22 significant bits), stacked as the two halves of
+// the MMA's N dimension. Each 32-weight block accumulates into its own TMEM
+// slot, and drainer warps apply the block scale in fp32:
+//   acc += d_b * (D_b,hi + D_b,lo) (+ m_b * sum_b x).
 // Products of small integers and fp16 values are exact in the fp32
 // accumulator, so the result equals the fp32 reference dot up to
 // accumulation-order rounding.
+//
+// Cost model (measured on B200): one tcgen05.mma with N <= 64 occupies the
+// SM's tensor pipe for ~44 cycles whatever its operands' source, and so does
+// a commit. A block of 128 rows x 32 weights therefore takes two MMAs
+// (K = 16 each, hi and lo in one instruction through N) and commits are
+// batched per group of G blocks. The tensor pipe queues only about two MMAs,
+// so the issuing thread must not stall: its loop is fully unrolled over a
+// quad with precomputed addresses, and a second issuer on another warp
+// scheduler covers the first one's barrier waits. Roles that wait off the
+// issue path sleep in the barrier (try_wait with a time hint) instead of
+// spinning, leaving the issue slots to the decoders and the issuers. The A operand is written by the decoders
+// straight into TMEM (tcgen05.st), which keeps the 2 B/weight of fp16 codes
+// off the shared-memory port entirely; shared memory only carries the packed
+// bytes and the activation tiles.
+//
+// K order inside a block. Decoder warp h (of the two per TMEM lane quarter)
+// writes the K pairs 8h..8h+7 of every block (the A operand of the block's
+// MMA h), taken from its own two 16-byte chunks of the lane-permuted weight
+// layout; an A slot is [h][block][8 columns]. The activation tile uses
+// the same order: column c = 4t + s of a block holds the original K pair
+// (8s + 2t, 8s + 2t + 1), for both the Q4 and the Q8 layouts.
 //
 // Persistent stream-K: one CTA per SM walks a contiguous range of the
 // tile-major (128-row tile, packed K step) space, so the weight stream never
 // restarts; a tile whose K loop is split across CTAs is completed by the last
 // contributor from at most two partial slots per CTA (deterministic order).
-// The tile is 128 weight rows (MMA M, TMEM lanes) x BN activation rows (MMA
-// N); a packed step is 8 quant blocks (256 K). Warp roles (16 warps; every
-// role that blocks on an mbarrier has a warp of its own, since a lane
-// suspended in try_wait holds up the diverged lanes of its warp):
-//   warp 0         TMA: packed quant rows (128-byte swizzle), PS stages;
-//   warp 1         TMEM allocation, single-thread MMA issue into the slot ring;
-//   warp 2         TMA: fp16 block scales (+ Q4_1 mins) of each step, SS stages;
-//   warp 3         TMA: fp16 activation hi/lo tiles, 64 K per MMA stage;
-//   warps 4..11    decoders: swizzled packed bytes -> exact fp16 codes in the
-//                  K-major 128-byte-swizzle layout of the A stage;
-//   warps 12..15   drainers: NB slots per batch, TMEM -> registers, one
-//                  tcgen05.wait::ld, free the slots, scale in fp32; flush per
-//                  tile (x row scale 2^-e, bias, store or partial + ticket).
+// A packed step is 8 quant blocks (256 K) = two quads of 4 blocks.
+// Warp roles (16 warps; every role that blocks on an mbarrier has a warp of
+// its own, since a lane suspended in try_wait holds up the diverged lanes of
+// its warp):
+//   warp 0         TMA: packed quant rows (128-byte swizzle, PS stages) and
+//                  the fp16 block scales (+ Q4_1 mins) of each step (SS stages);
+//   warps 1, 3     TMEM allocation (warp 1); MMA issue from one thread each,
+//                  alternate quads, one commit per group;
+//   warp 2         TMA: fp16 activation tiles (hi rows, lo rows), one per quad;
+//   warps 4..11    decoders: two per TMEM lane quarter, one per K half of
+//                  every block; packed bytes -> exact fp16 codes -> one
+//                  tcgen05.st per quad into the A ring (one quad a slot);
+//   warps 12..15   drainers: per group, TMEM -> registers, scale in fp32;
+//                  flush per tile (x row scale 2^-e, bias, store or partial +
+//                  ticket).
 // Every wait is bounded in time; a timeout raises the CTA abort flag and the
 // host-visible error flag, and all roles leave their loops (the drainers keep
-// their loop shape so that their named barriers still match).
+// their loop shape so that their named barriers still match). Before the TMEM
+// is released the MMA thread waits for its last commit and the TMA threads
+// for their copies in flight.
 #pragma once
 
 #include <cuda.h>
@@ -50,6 +76,7 @@ constexpr int kDecRows = 128;
 constexpr int kDecWarps = 16;
 constexpr int kDecThreads = kDecWarps * 32;
 constexpr int kDecBlocksPerStep = 8;  // quant blocks per packed step (Q4_x: 128 B per row, Q8_0: 256 B)
+constexpr int kDecGroupBars = 16;     // commit barriers, one per group in a ring
 constexpr uint64_t kDecWaitNs = 1000000000ull;
 constexpr uint64_t kDecDrainNs = 20000000ull;
 
@@ -71,23 +98,36 @@ struct DecArgs {
 
 template <int QT, int BN>
 struct DecCfg {
+  static constexpr int N = 2 * BN;    // MMA N: hi rows, then lo rows
+  static constexpr int G = 64 / N;     // blocks per commit group: a group's D is 64 TMEM columns
+  static constexpr int NA = 4;         // A quads in TMEM (64 columns each)
+  static constexpr int ND = 4;         // D groups in TMEM
+  static constexpr int kACols = 64;
+  static constexpr int kDCols = G * N;
+  static constexpr int kDOff = NA * kACols;
+  static_assert(kDCols == 64 && kDOff + ND * kDCols <= 512, "TMEM budget");
+  // Parity waits on the commit ring must not alias: a decoder waits for the
+  // last group of quad q - NA while quads up to q - 1 may have committed.
+  static_assert(kDecGroupBars > (4 / G) * (NA - 1), "commit ring too short");
   static constexpr int kPkBytes = kDecRows * (QT == MQ_Q8_0 ? 256 : 128);  // packed step
   static constexpr int kScBytes = kDecRows * 16 * (QT == MQ_Q4_1 ? 2 : 1);  // scales (+ mins) of a step
+  static constexpr int kXBytes = N * 128 * 2;                               // activation tile of a quad (128 K)
   static constexpr int PS = QT == MQ_Q8_0 ? 3 : 4;  // packed stages
-  static constexpr int SS = 12;                     // scale stages
-  static constexpr int AS = 4;                      // A / activation stages (64 K each)
-  static constexpr int R = 512 / BN;                // TMEM slots (one per block in flight)
-  static constexpr int NB = BN == 16 ? 4 : 1;       // blocks per drain batch
-  static constexpr int kA = kDecRows * 64 * 2;      // fp16 codes, 64 K
-  static constexpr int kX = BN * 64 * 2;            // fp16 activation tile (hi or lo)
+  static constexpr int SS = 6;                      // scale stages
+  static constexpr int XS = 4;                      // activation stages (one quad each)
   static constexpr int kPkOff = 0;
   static constexpr int kScOff = kPkOff + PS * kPkBytes;
-  static constexpr int kAOff = kScOff + SS * kScBytes;
-  static constexpr int kXOff = kAOff + AS * kA;
-  static constexpr int kBarOff = kXOff + AS * 2 * kX;
-  static constexpr int kNumBars = 2 * PS + 2 * SS + 3 * AS + 2 * R;
+  static constexpr int kXOff = kScOff + SS * kScBytes;
+  static constexpr int kBarOff = kXOff + XS * kXBytes;
+  static constexpr int kQuadsPerUnit = 1;            // an MMA issuer's unit: one quad (whole groups)
+  // Two issuers take alternate quads. With G = 1 a quad's four groups use
+  // every D slot, so both issuers would wait on the same slots: one issuer.
+  static constexpr int kIssuers = G == 1 ? 1 : 2;
+  static constexpr int kNumBars = 2 * PS + 2 * SS + XS + NA + ND + kDecGroupBars + 2;
   static constexpr int kBytes = kBarOff + 8 * kNumBars + 16;
-  static constexpr int kAlloc = kBytes + 1024;
+  // At least 116 KB, so that a second CTA (and its 512-column TMEM request)
+  // never lands on an SM this kernel already occupies.
+  static constexpr int kAlloc = (kBytes + 1024) > 118784 ? (kBytes + 1024) : 118784;
   static_assert(kAlloc <= 227 * 1024, "shared memory budget");
 };
 
@@ -118,10 +158,33 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
   return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-  sm100::umma_bf16(tmem_d, adesc, bdesc, idesc, accumulate);  // same instruction; formats live in idesc
+// D[tmem] (+)= A[tmem] x B[smem]^T, kind::f16, A read from tensor memory.
+__device__ __forceinline__ void umma_f16_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
+
+__device__ __forceinline__ void tmem_st_x8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
@@ -132,50 +195,56 @@ __device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
-__device__ __forceinline__ void tmem_ld_x4(uint32_t taddr, uint32_t (&r)[4]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(taddr));
-}
-template <int NC>
-__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[NC]) {
-  if constexpr (NC == 4) tmem_ld_x4(taddr, r);
-  else if constexpr (NC == 16) tmem_ld_x16(taddr, r);
-  else sm100::tmem_ld_32x32b_x32(taddr, r);
+// N consecutive 32-bit columns of this warp's 32 lanes.
+template <int N>
+__device__ __forceinline__ void tmem_ld_n(uint32_t taddr, uint32_t (&r)[N]) {
+  if constexpr (N == 16) {
+    tmem_ld_x16(taddr, r);
+  } else if constexpr (N == 32) {
+    sm100::tmem_ld_32x32b_x32(taddr, r);
+  } else {
+    static_assert(N == 64, "activation tile width");
+    sm100::tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+    sm100::tmem_ld_32x32b_x32(taddr + 32u, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+  }
 }
 
 template <int QT, int BN, int NC>
 __global__ void __launch_bounds__(kDecThreads, 1)
     tcdec_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_d,
-                 const __grid_constant__ CUtensorMap tm_m, const __grid_constant__ CUtensorMap tm_xh,
-                 const __grid_constant__ CUtensorMap tm_xl, const DecArgs a) {
+                 const __grid_constant__ CUtensorMap tm_m, const __grid_constant__ CUtensorMap tm_x,
+                 const DecArgs a) {
   using L = DecCfg<QT, BN>;
-  constexpr int PS = L::PS, SS = L::SS, AS = L::AS, R = L::R, NB = L::NB;
+  constexpr int PS = L::PS, SS = L::SS, XS = L::XS, NA = L::NA, ND = L::ND, G = L::G, N = L::N;
+  constexpr int NGB = kDecGroupBars;
+  constexpr int kGroupsPerStep = kDecBlocksPerStep / G;
+  constexpr int kQPU = L::kQuadsPerUnit, NI = L::kIssuers;
+  static_assert(NC <= BN && NC % 4 == 0, "live activation columns");
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::kBarOff);
   uint64_t *pk_full = bars, *pk_empty = pk_full + PS;
   uint64_t *sc_full = pk_empty + PS, *sc_empty = sc_full + SS;
-  uint64_t *a_full = sc_empty + SS, *x_full = a_full + AS, *a_empty = x_full + AS;
-  uint64_t *s_full = a_empty + AS, *s_empty = s_full + R;
+  uint64_t *x_full = sc_empty + SS, *a_full = x_full + XS, *d_empty = a_full + NA;
+  uint64_t *grp_done = d_empty + ND, *fin = grp_done + NGB;  // fin: one per issuer
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::kNumBars);
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
   __shared__ int s_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int S = a.steps, T = a.tiles * a.steps, G = gridDim.x, cta = blockIdx.x;
-  const int g0 = dec_first_step(cta, G, T), g1 = dec_first_step(cta + 1, G, T);
+  const int S = a.steps, T = a.tiles * a.steps, GR = gridDim.x, cta = blockIdx.x;
+  const int g0 = dec_first_step(cta, GR, T), g1 = dec_first_step(cta + 1, GR, T);
   const int nsteps = g1 - g0;
+  const int nquads = 2 * nsteps;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < PS; ++i) sm100::mbar_init(&pk_full[i], 1), sm100::mbar_init(&pk_empty[i], 256);
-    for (int i = 0; i < SS; ++i) sm100::mbar_init(&sc_full[i], 1), sm100::mbar_init(&sc_empty[i], 128);
-    for (int i = 0; i < AS; ++i) {
-      sm100::mbar_init(&a_full[i], 256);
-      sm100::mbar_init(&x_full[i], 1);
-      sm100::mbar_init(&a_empty[i], 1);
-    }
-    for (int i = 0; i < R; ++i) sm100::mbar_init(&s_full[i], 1), sm100::mbar_init(&s_empty[i], 128);
+    for (int i = 0; i < PS; ++i) sm100::mbar_init(&pk_full[i], 1), sm100::mbar_init(&pk_empty[i], 8);
+    for (int i = 0; i < SS; ++i) sm100::mbar_init(&sc_full[i], 1), sm100::mbar_init(&sc_empty[i], 4);
+    for (int i = 0; i < XS; ++i) sm100::mbar_init(&x_full[i], 1);
+    for (int i = 0; i < NA; ++i) sm100::mbar_init(&a_full[i], 8);
+    for (int i = 0; i < ND; ++i) sm100::mbar_init(&d_empty[i], 4);
+    for (int i = 0; i < NGB; ++i) sm100::mbar_init(&grp_done[i], 1);
+    for (int i = 0; i < 2; ++i) sm100::mbar_init(&fin[i], 1);
     *abort = 0;
     sm100::fence_mbar_init();
   }
@@ -188,14 +257,20 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // Commit group of the last block of quad q: its completion frees the quad's
+  // A slot and activation stage.
+  auto quad_group = [&](int q) { return (4 * q + 3) / G; };
+
   if (warp == 0) {
-    if (lane == 0) {  // ------------------------------------- TMA: packed quant rows
+    if (lane == 0) {  // ------------------------------------- TMA: packed quant rows and their scales
       sm100::prefetch_tmap(&tm_q);
-      int issued = 0;
+      sm100::prefetch_tmap(&tm_d);
+      if (QT == MQ_Q4_1) sm100::prefetch_tmap(&tm_m);
+      int issued_pk = 0, issued_sc = 0;
       for (int ls = 0; ls < nsteps; ++ls) {
-        const int i = ls % PS;
-        if (!sm100::mbar_wait(&pk_empty[i], ((uint32_t)(ls / PS) & 1u) ^ 1u, a.err, abort, kDecWaitNs)) break;
         const int g = g0 + ls, t = g / S, k = g % S;
+        const int i = ls % PS;
+        if (!sm100::mbar_wait_sleep(&pk_empty[i], ((uint32_t)(ls / PS) & 1u) ^ 1u, a.err, abort, kDecWaitNs)) break;
         uint8_t *dst = smem + L::kPkOff + i * L::kPkBytes;
         sm100::mbar_arrive_expect_tx(&pk_full[i], L::kPkBytes);
         if constexpr (QT == MQ_Q8_0) {
@@ -204,154 +279,169 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         } else {
           sm100::tma_load_2d(dst, &tm_q, k * 128, t * kDecRows, &pk_full[i]);
         }
-        issued = ls + 1;
-      }
-      for (int p = issued - PS < 0 ? 0 : issued - PS; p < issued; ++p)
-        sm100::mbar_wait(&pk_full[p % PS], (uint32_t)(p / PS) & 1u, nullptr, nullptr, kDecDrainNs);
-    }
-  } else if (warp == 2) {
-    if (lane == 0) {  // ------------------------------------- TMA: block scales (+ Q4_1 mins)
-      sm100::prefetch_tmap(&tm_d);
-      if (QT == MQ_Q4_1) sm100::prefetch_tmap(&tm_m);
-      int issued = 0;
-      for (int ls = 0; ls < nsteps; ++ls) {
-        const int i = ls % SS;
-        if (!sm100::mbar_wait(&sc_empty[i], ((uint32_t)(ls / SS) & 1u) ^ 1u, a.err, abort, kDecWaitNs)) break;
-        const int g = g0 + ls, t = g / S, k = g % S;
-        uint8_t *dst = smem + L::kScOff + i * L::kScBytes;
-        sm100::mbar_arrive_expect_tx(&sc_full[i], L::kScBytes);
-        sm100::tma_load_2d(dst, &tm_d, k * kDecBlocksPerStep, t * kDecRows, &sc_full[i]);
+        issued_pk = ls + 1;
+        const int j = ls % SS;
+        if (!sm100::mbar_wait_sleep(&sc_empty[j], ((uint32_t)(ls / SS) & 1u) ^ 1u, a.err, abort, kDecWaitNs)) break;
+        uint8_t *sdst = smem + L::kScOff + j * L::kScBytes;
+        sm100::mbar_arrive_expect_tx(&sc_full[j], L::kScBytes);
+        sm100::tma_load_2d(sdst, &tm_d, k * kDecBlocksPerStep, t * kDecRows, &sc_full[j]);
         if constexpr (QT == MQ_Q4_1)
-          sm100::tma_load_2d(dst + kDecRows * 16, &tm_m, k * kDecBlocksPerStep, t * kDecRows, &sc_full[i]);
-        issued = ls + 1;
+          sm100::tma_load_2d(sdst + kDecRows * 16, &tm_m, k * kDecBlocksPerStep, t * kDecRows, &sc_full[j]);
+        issued_sc = ls + 1;
       }
-      for (int p = issued - SS < 0 ? 0 : issued - SS; p < issued; ++p)
+      for (int p = issued_pk - PS < 0 ? 0 : issued_pk - PS; p < issued_pk; ++p)
+        sm100::mbar_wait(&pk_full[p % PS], (uint32_t)(p / PS) & 1u, nullptr, nullptr, kDecDrainNs);
+      for (int p = issued_sc - SS < 0 ? 0 : issued_sc - SS; p < issued_sc; ++p)
         sm100::mbar_wait(&sc_full[p % SS], (uint32_t)(p / SS) & 1u, nullptr, nullptr, kDecDrainNs);
     }
-  } else if (warp == 3) {
-    if (lane == 0) {  // ------------------------------------- TMA: activation hi/lo tiles
-      sm100::prefetch_tmap(&tm_xh);
-      sm100::prefetch_tmap(&tm_xl);
+  } else if (warp == 2) {
+    if (lane == 0) {  // ------------------------------------- TMA: activation tiles, one per quad
+      sm100::prefetch_tmap(&tm_x);
       int issued = 0;
-      const int nst = 4 * nsteps;
-      for (int s = 0; s < nst; ++s) {
-        const int i = s % AS;
-        if (!sm100::mbar_wait(&a_empty[i], ((uint32_t)(s / AS) & 1u) ^ 1u, a.err, abort, kDecWaitNs)) break;
-        const int k = (g0 + s / 4) % S;
-        const int kx = (k * kDecBlocksPerStep + 2 * (s % 4)) * 32;
-        uint8_t *dst = smem + L::kXOff + i * 2 * L::kX;
-        sm100::mbar_arrive_expect_tx(&x_full[i], 2 * L::kX);
-        sm100::tma_load_2d(dst, &tm_xh, kx, 0, &x_full[i]);
-        sm100::tma_load_2d(dst + L::kX, &tm_xl, kx, 0, &x_full[i]);
-        issued = s + 1;
+      for (int q = 0; q < nquads; ++q) {
+        const int i = q % XS;
+        if (q >= XS) {  // the stage is free once the MMAs of quad q - XS completed
+          const int gq = quad_group(q - XS);
+          if (!sm100::mbar_wait_sleep(&grp_done[gq % NGB], (uint32_t)(gq / NGB) & 1u, a.err, abort, kDecWaitNs))
+            break;
+        }
+        const int k = (g0 + q / 2) % S;
+        const int kx = (k * kDecBlocksPerStep + 4 * (q & 1)) * 32;
+        uint8_t *dst = smem + L::kXOff + i * L::kXBytes;
+        sm100::mbar_arrive_expect_tx(&x_full[i], L::kXBytes);
+        sm100::tma_load_2d(dst, &tm_x, kx, 0, &x_full[i]);
+        sm100::tma_load_2d(dst + N * 128, &tm_x, kx + 64, 0, &x_full[i]);
+        issued = q + 1;
       }
-      for (int s = issued - AS < 0 ? 0 : issued - AS; s < issued; ++s)
-        sm100::mbar_wait(&x_full[s % AS], (uint32_t)(s / AS) & 1u, nullptr, nullptr, kDecDrainNs);
+      for (int q = issued - XS < 0 ? 0 : issued - XS; q < issued; ++q)
+        sm100::mbar_wait(&x_full[q % XS], (uint32_t)(q / XS) & 1u, nullptr, nullptr, kDecDrainNs);
     }
-  } else if (warp == 1) {
-    if (lane == 0) {  // ------------------------------------- MMA issue into the TMEM slot ring
-      constexpr uint32_t idesc = idesc_f16_f32(kDecRows, BN);
-      const int nst = 4 * nsteps;
-      for (int s = 0; s < nst; ++s) {
-        const int i = s % AS;
-        const uint32_t ph = (uint32_t)(s / AS) & 1u;
-        if (!sm100::mbar_wait(&a_full[i], ph, a.err, abort, kDecWaitNs)) break;
-        if (!sm100::mbar_wait(&x_full[i], ph, a.err, abort, kDecWaitNs)) break;
-        sm100::tc_fence_after();
-        const uint32_t abase = sm100::smem_u32(smem + L::kAOff + i * L::kA);
-        const uint32_t xbase = sm100::smem_u32(smem + L::kXOff + i * 2 * L::kX);
-        const uint64_t da = sm100::umma_desc_sw128(abase);
-        const uint64_t dh = sm100::umma_desc_sw128(xbase), dl = sm100::umma_desc_sw128(xbase + L::kX);
+  } else if (warp == 1 || warp == 3) {
+    const int issuer = warp >> 1;  // warp 1: units 0, 2, 4, ...; warp 3: units 1, 3, 5, ...
+    if (lane == 0 && issuer < NI) {  // ------------------------- MMA issue, one commit per group
+      // A unit is one quad (two when a commit group spans two quads). The two
+      // issuers sit on different warp schedulers and take alternate units, so
+      // that one issues while the other waits. Every barrier slot an issuer
+      // waits on was last waited on by the same issuer, or completes in order
+      // with one it has waited on, so parity waits never alias.
+      constexpr uint32_t idesc = idesc_f16_f32(kDecRows, N);
+      const int nunits = nquads / kQPU;
+      for (int u = issuer; u < nunits; u += NI) {
         bool ok = true;
+        uint32_t abase[kQPU];
+        uint64_t xdesc[kQPU];
 #pragma unroll
-        for (int blk = 0; blk < 2; ++blk) {
-          const int b = 2 * s + blk;
-          const int slot = b % R;
-          if (!sm100::mbar_wait(&s_empty[slot], ((uint32_t)(b / R) & 1u) ^ 1u, a.err, abort, kDecWaitNs)) {
+        for (int qi = 0; qi < kQPU; ++qi) {
+          const int q = u * kQPU + qi;
+          ok = ok && sm100::mbar_wait(&a_full[q % NA], (uint32_t)(q / NA) & 1u, a.err, abort, kDecWaitNs);
+          ok = ok && sm100::mbar_wait(&x_full[q % XS], (uint32_t)(q / XS) & 1u, a.err, abort, kDecWaitNs);
+          abase[qi] = tmem + (uint32_t)((q % NA) * L::kACols);
+          xdesc[qi] = sm100::umma_desc_sw128(sm100::smem_u32(smem + L::kXOff + (q % XS) * L::kXBytes));
+        }
+        if (!ok) break;
+        uint32_t dbase = 0;
+#pragma unroll
+        for (int bl = 0; bl < 4 * kQPU; ++bl) {
+          const int qi = bl >> 2, jq = bl & 3;
+          const int b = u * 4 * kQPU + bl;
+          const int jg = bl % G;  // units start on group boundaries
+          if (jg == 0) {
+            const int gi = b / G;
+            if (!sm100::mbar_wait(&d_empty[gi % ND], ((uint32_t)(gi / ND) & 1u) ^ 1u, a.err, abort, kDecWaitNs)) {
+              ok = false;
+              break;
+            }
+            sm100::tc_fence_after();
+            dbase = tmem + (uint32_t)(L::kDOff + (gi % ND) * L::kDCols);
+          }
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            constexpr int kRow = N * 128;  // bytes of one 64-K atom column of the activation tile
+            const int kk = 32 * jq + 16 * h;
+            const uint32_t off = (uint32_t)((kk >> 6) * kRow + (kk & 63) * 2);
+            umma_f16_tmem_a(dbase + (uint32_t)(jg * N), abase[qi] + (uint32_t)(32 * h + 8 * jq),
+                            xdesc[qi] + (off >> 4), idesc, (uint32_t)h);
+          }
+          if (jg == G - 1) sm100::umma_commit(&grp_done[(b / G) % NGB]);
+        }
+        if (!ok) break;
+      }
+      // Everything issued has completed before the TMEM is released.
+      sm100::umma_commit(&fin[issuer]);
+      sm100::mbar_wait(&fin[issuer], 0u, nullptr, nullptr, kDecDrainNs);
+    }
+  } else if (warp < 12) {  // -------------------------------- decoders: packed bytes -> exact fp16 codes in TMEM
+    const int qq = warp & 3;          // TMEM lane quarter
+    const int hh = (warp - 4) >> 2;   // K half of every block: A columns 32hh..32hh+31 of a slot
+    const int r = 32 * qq + lane;     // tile row
+    const int sw = r & 7;
+    const uint32_t lane_base = (uint32_t)(32 * qq) << 16;
+    for (int ls = 0; ls < nsteps; ++ls) {
+      const int pi = ls % PS;
+      // tcgen05.st is warp-collective: every wait result is made warp-uniform.
+      if (!__all_sync(0xffffffffu,
+                      sm100::mbar_wait_sleep(&pk_full[pi], (uint32_t)(ls / PS) & 1u, a.err, abort, kDecWaitNs)))
+        break;
+      bool ok = true;
+#pragma unroll 1
+      for (int qi = 0; qi < 2; ++qi) {
+        const int q = 2 * ls + qi;
+        if (q >= NA) {  // the A slot is free once the MMAs of quad q - NA completed
+          const int gq = quad_group(q - NA);
+          if (!__all_sync(0xffffffffu, sm100::mbar_wait_sleep(&grp_done[gq % NGB], (uint32_t)(gq / NGB) & 1u, a.err,
+                                                              abort, kDecWaitNs))) {
             ok = false;
             break;
           }
-          sm100::tc_fence_after();
-          const uint32_t d = tmem + (uint32_t)(slot * BN);
-#pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            const uint64_t off = (uint64_t)(2 * (2 * blk + k));  // 32-byte K steps, in 16-byte units
-            umma_f16(d, da + off, dh + off, idesc, k);
-            umma_f16(d, da + off, dl + off, idesc, 1u);
-          }
-          sm100::umma_commit(&s_full[slot]);
         }
-        sm100::umma_commit(&a_empty[i]);
-        if (!ok) break;
-      }
-    }
-  } else if (warp < 12) {  // -------------------------------- decoders: packed bytes -> exact fp16 codes
-    const int t256 = threadIdx.x - 128;
-    const int r = t256 & 127;  // tile row
-    const int h = t256 >> 7;   // group h of the step: MMA stages 2h, 2h+1
-    const int sw = r & 7;
-    for (int ls = 0; ls < nsteps; ++ls) {
-      const int pi = ls % PS;
-      if (!sm100::mbar_wait(&pk_full[pi], (uint32_t)(ls / PS) & 1u, a.err, abort, kDecWaitNs)) break;
-      bool ok = true;
-      for (int q = 0; q < 4; ++q) {
-        const int s = 4 * ls + q;
-        const int i = s % AS;
-        if (!sm100::mbar_wait(&a_empty[i], ((uint32_t)(s / AS) & 1u) ^ 1u, a.err, abort, kDecWaitNs)) {
-          ok = false;
-          break;
-        }
-        if ((q >> 1) == h) {
-          const int sub = q & 1;  // blocks 2*sub, 2*sub+1 of group h
-          uint8_t *arow = smem + L::kAOff + i * L::kA + r * 128;
-          if constexpr (QT == MQ_Q8_0) {
-            const uint8_t *prow = smem + L::kPkOff + pi * L::kPkBytes + h * (kDecRows * 128) + r * 128;
-            uint32_t *o = reinterpret_cast<uint32_t *>(arow);
+        uint32_t col[32];  // [block j][8 columns]: K pairs 16hh..16hh+15 of every block
+        if constexpr (QT == MQ_Q8_0) {
+          const uint8_t *prow = smem + L::kPkOff + pi * L::kPkBytes + qi * (kDecRows * 128) + r * 128;
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              const uint4 c = *reinterpret_cast<const uint4 *>(prow + (((2 * t + sub) ^ sw) << 4));
-              const uint32_t u[2][2] = {{c.x ^ 0x80808080u, c.y ^ 0x80808080u}, {c.z ^ 0x80808080u, c.w ^ 0x80808080u}};
+          for (int tt = 0; tt < 2; ++tt) {
+            const int t = 2 * hh + tt;
+            const uint4 c0 = *reinterpret_cast<const uint4 *>(prow + (((2 * t) ^ sw) << 4));      // blocks 0, 1
+            const uint4 c1 = *reinterpret_cast<const uint4 *>(prow + (((2 * t + 1) ^ sw) << 4));  // blocks 2, 3
+            const uint32_t wv[4][2] = {{c0.x, c0.y}, {c0.z, c0.w}, {c1.x, c1.y}, {c1.z, c1.w}};
 #pragma unroll
-              for (int bl = 0; bl < 2; ++bl) {
-                o[(((4 * bl + 0) ^ sw) << 2) + t] = dcode_q8(u[bl][0], 0x4140u);
-                o[(((4 * bl + 1) ^ sw) << 2) + t] = dcode_q8(u[bl][0], 0x4342u);
-                o[(((4 * bl + 2) ^ sw) << 2) + t] = dcode_q8(u[bl][1], 0x4140u);
-                o[(((4 * bl + 3) ^ sw) << 2) + t] = dcode_q8(u[bl][1], 0x4342u);
-              }
-            }
-          } else {
-            const uint8_t *prow = smem + L::kPkOff + pi * L::kPkBytes + r * 128;
-            uint4 c[4];
-#pragma unroll
-            for (int t = 0; t < 4; ++t) c[t] = *reinterpret_cast<const uint4 *>(prow + (((4 * h + t) ^ sw) << 4));
-#pragma unroll
-            for (int bl = 0; bl < 2; ++bl) {
-              const int j = 2 * sub + bl;
-              uint4 oc[4];
-#pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                const uint32_t wd = j == 0 ? c[t].x : j == 1 ? c[t].y : j == 2 ? c[t].z : c[t].w;
-                const uint32_t v0 = dcode_q4<QT>(wd, 0), v1 = dcode_q4<QT>(wd, 8);
-                const uint32_t v2 = dcode_q4<QT>(wd, 4), v3 = dcode_q4<QT>(wd, 12);
-                (t == 0 ? oc[0].x : t == 1 ? oc[0].y : t == 2 ? oc[0].z : oc[0].w) = v0;
-                (t == 0 ? oc[1].x : t == 1 ? oc[1].y : t == 2 ? oc[1].z : oc[1].w) = v1;
-                (t == 0 ? oc[2].x : t == 1 ? oc[2].y : t == 2 ? oc[2].z : oc[2].w) = v2;
-                (t == 0 ? oc[3].x : t == 1 ? oc[3].y : t == 2 ? oc[3].z : oc[3].w) = v3;
-              }
-#pragma unroll
-              for (int u = 0; u < 4; ++u) *reinterpret_cast<uint4 *>(arow + (((4 * bl + u) ^ sw) << 4)) = oc[u];
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t u0 = wv[j][0] ^ 0x80808080u, u1 = wv[j][1] ^ 0x80808080u;
+              col[8 * j + 4 * tt + 0] = dcode_q8(u0, 0x4140u);
+              col[8 * j + 4 * tt + 1] = dcode_q8(u0, 0x4342u);
+              col[8 * j + 4 * tt + 2] = dcode_q8(u1, 0x4140u);
+              col[8 * j + 4 * tt + 3] = dcode_q8(u1, 0x4342u);
             }
           }
-          sm100::fence_proxy_async_smem();
+        } else {
+          const uint8_t *prow = smem + L::kPkOff + pi * L::kPkBytes + r * 128;
+#pragma unroll
+          for (int tt = 0; tt < 2; ++tt) {
+            const int t = 2 * hh + tt;
+            const uint4 c = *reinterpret_cast<const uint4 *>(prow + (((4 * qi + t) ^ sw) << 4));
+            const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              col[8 * j + 4 * tt + 0] = dcode_q4<QT>(wv[j], 0);
+              col[8 * j + 4 * tt + 1] = dcode_q4<QT>(wv[j], 8);
+              col[8 * j + 4 * tt + 2] = dcode_q4<QT>(wv[j], 4);
+              col[8 * j + 4 * tt + 3] = dcode_q4<QT>(wv[j], 12);
+            }
+          }
         }
-        sm100::mbar_arrive(&a_full[i]);
+        tmem_st_x32(tmem + lane_base + (uint32_t)((q % NA) * L::kACols + 32 * hh), col);
+        tmem_st_wait();
+        sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&a_full[q % NA]);
       }
       if (!ok) break;
-      sm100::mbar_arrive(&pk_empty[pi]);
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&pk_empty[pi]);
     }
   } else {  // ------------------------------------------------ drainers (TMEM lane = tile row)
-    const int r = 32 * (warp & 3) + lane;
-    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    const int qq = warp & 3;
+    const int r = 32 * qq + lane;
+    const uint32_t lane_base = (uint32_t)(32 * qq) << 16;
     float acc[NC];
     int cur = -1;
     // Completes the tile's output: directly when this CTA owns the whole K loop
@@ -383,7 +473,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         *reinterpret_cast<float4 *>(slot + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
       __threadfence();
       asm volatile("bar.sync 1, 128;" ::: "memory");
-      const int cf = dec_cta_of_step(tg0, G, T), cl = dec_cta_of_step(tg1 - 1, G, T);
+      const int cf = dec_cta_of_step(tg0, GR, T), cl = dec_cta_of_step(tg1 - 1, GR, T);
       if (warp == 12 && lane == 0) s_last = atomicAdd(&a.tickets[tile], 1) == cl - cf;
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (s_last) {
@@ -392,7 +482,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 #pragma unroll
         for (int c = 0; c < NC; ++c) tot[c] = 0.0f;
         for (int cc = cf; cc <= cl; ++cc) {  // fixed CTA order: deterministic
-          const int kk = (tile == dec_first_step(cc, G, T) / S) ? 0 : 1;
+          const int kk = (tile == dec_first_step(cc, GR, T) / S) ? 0 : 1;
           const float *ps = a.partial + (((int64_t)cc * 2 + kk) * kDecRows + r) * BN;
 #pragma unroll
           for (int c = 0; c < NC; c += 4) {
@@ -422,54 +512,54 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       const int si = ls % SS;
       // Failed waits do not leave the loop: every drainer must run the same
       // sequence of flushes (they synchronise on a named barrier).
-      bool ok = sm100::mbar_wait(&sc_full[si], (uint32_t)(ls / SS) & 1u, a.err, abort, kDecWaitNs);
+      const bool sc_ok = sm100::mbar_wait_sleep(&sc_full[si], (uint32_t)(ls / SS) & 1u, a.err, abort, kDecWaitNs);
       const uint8_t *sc = smem + L::kScOff + si * L::kScBytes;
       const uint4 dq = *reinterpret_cast<const uint4 *>(sc + r * 16);
       uint4 mq = make_uint4(0u, 0u, 0u, 0u);
       if constexpr (QT == MQ_Q4_1) mq = *reinterpret_cast<const uint4 *>(sc + kDecRows * 16 + r * 16);
+      const uint32_t dw[4] = {dq.x, dq.y, dq.z, dq.w};
+      const uint32_t mw[4] = {mq.x, mq.y, mq.z, mq.w};
 #pragma unroll
-      for (int bb = 0; bb < kDecBlocksPerStep; bb += NB) {
-        int slots[NB];
-#pragma unroll
-        for (int j = 0; j < NB; ++j) {
-          const int b = kDecBlocksPerStep * ls + bb + j;
-          slots[j] = b % R;
-          ok = sm100::mbar_wait(&s_full[slots[j]], (uint32_t)(b / R) & 1u, a.err, abort, kDecWaitNs) && ok;
-        }
-        ok = __all_sync(0xffffffffu, ok);
-        uint32_t v[NB][NC];
+      for (int gl = 0; gl < kGroupsPerStep; ++gl) {
+        const int gi = ls * kGroupsPerStep + gl;
+        bool ok = sm100::mbar_wait_sleep(&grp_done[gi % NGB], (uint32_t)(gi / NGB) & 1u, a.err, abort, kDecWaitNs);
+        ok = __all_sync(0xffffffffu, ok && sc_ok);
+        sm100::tc_fence_after();
+        const uint32_t dbase = tmem + lane_base + (uint32_t)(L::kDOff + (gi % ND) * L::kDCols);
+        // The whole group in one batch of loads and one wait; the D slot is
+        // released before the arithmetic.
+        uint32_t v[G * N];
         if (ok) {
-          sm100::tc_fence_after();
 #pragma unroll
-          for (int j = 0; j < NB; ++j) tmem_ld_cols<NC>(tmem + lane_base + (uint32_t)(slots[j] * BN), v[j]);
+          for (int jg = 0; jg < G; ++jg)
+            tmem_ld_n<N>(dbase + (uint32_t)(jg * N), *reinterpret_cast<uint32_t(*)[N]>(&v[jg * N]));
           sm100::tmem_ld_wait();
         } else {
 #pragma unroll
-          for (int j = 0; j < NB; ++j)
-#pragma unroll
-            for (int c = 0; c < NC; ++c) v[j][c] = 0u;
+          for (int c = 0; c < G * N; ++c) v[c] = 0u;
         }
         sm100::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&d_empty[gi % ND]);
 #pragma unroll
-        for (int j = 0; j < NB; ++j) sm100::mbar_arrive(&s_empty[slots[j]]);
-#pragma unroll
-        for (int j = 0; j < NB; ++j) {
-          const int jb = bb + j;
-          const uint32_t dw = jb < 4 ? (jb < 2 ? dq.x : dq.y) : (jb < 6 ? dq.z : dq.w);
-          const __half2 d2 = *reinterpret_cast<const __half2 *>(&dw);
+        for (int jg = 0; jg < G; ++jg) {
+          const int jb = gl * G + jg;  // block of the step
+          const uint32_t *vb = &v[jg * N];
+          const __half2 d2 = *reinterpret_cast<const __half2 *>(&dw[jb >> 1]);
           const float d = (jb & 1) ? __high2float(d2) : __low2float(d2);
 #pragma unroll
           for (int c = 0; c < NC; c += 2) {
-            const float2 r2 = __ffma2_rn(make_float2(d, d),
-                                         make_float2(__uint_as_float(v[j][c]), __uint_as_float(v[j][c + 1])),
-                                         make_float2(acc[c], acc[c + 1]));
+            float2 r2 = __ffma2_rn(make_float2(d, d), make_float2(__uint_as_float(vb[c]), __uint_as_float(vb[c + 1])),
+                                   make_float2(acc[c], acc[c + 1]));
+            r2 = __ffma2_rn(make_float2(d, d),
+                            make_float2(__uint_as_float(vb[BN + c]), __uint_as_float(vb[BN + c + 1])), r2);
             acc[c] = r2.x, acc[c + 1] = r2.y;
           }
           if constexpr (QT == MQ_Q4_1) {
-            const uint32_t mw = jb < 4 ? (jb < 2 ? mq.x : mq.y) : (jb < 6 ? mq.z : mq.w);
-            const __half2 m2 = *reinterpret_cast<const __half2 *>(&mw);
+            const __half2 m2 = *reinterpret_cast<const __half2 *>(&mw[jb >> 1]);
             const float mm = (jb & 1) ? __high2float(m2) : __low2float(m2);
-            const float4 *xs = reinterpret_cast<const float4 *>(a.xsum + (int64_t)(kstep * kDecBlocksPerStep + jb) * BN);
+            const float4 *xs =
+                reinterpret_cast<const float4 *>(a.xsum + (int64_t)(kstep * kDecBlocksPerStep + jb) * BN);
 #pragma unroll
             for (int c = 0; c < NC; c += 4) {
               const float4 s4 = __ldg(xs + c / 4);
@@ -481,7 +571,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
           }
         }
       }
-      sm100::mbar_arrive(&sc_empty[si]);
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&sc_empty[si]);
     }
     if (cur >= 0) flush(cur);
   }
@@ -496,11 +587,13 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 
 // Activation split for the decode GEMM: one CTA per activation row (rows >= m
 // become zeros). Row i is scaled by 2^e_i (largest magnitude in [2^13, 2^14)),
-// split into fp16 hi + lo, K-major [BN][kpad] for TMA; block sums (Q4_1) and
-// 2^-e_i are written alongside.
+// split into fp16 hi + lo and written K-major into x2 ([2 bn][kpad]: hi rows,
+// then lo rows) in the decode kernel's K order (column c = 4t + s of a
+// block holds the original pair 8s + 2t, 8s + 2t + 1); block sums (Q4_1, in
+// natural order) and 2^-e_i are written alongside.
 __global__ void dec_prep_kernel(const float *__restrict__ x, int64_t ldx, int m, int K, int kpad, int bn,
-                                __half *__restrict__ xh, __half *__restrict__ xl, float *__restrict__ xsum,
-                                float *__restrict__ xinv, int want_sums) {
+                                __half *__restrict__ x2, float *__restrict__ xsum, float *__restrict__ xinv,
+                                int want_sums) {
   const int row = blockIdx.x;
   const bool live = row < m;
   const float *xr = x + (int64_t)(live ? row : 0) * ldx;
@@ -526,14 +619,15 @@ __global__ void dec_prep_kernel(const float *__restrict__ x, int64_t ldx, int m,
   }
   __syncthreads();
   const float sc = s_scale;
-  __half2 *h2 = reinterpret_cast<__half2 *>(xh + (int64_t)row * kpad);
-  __half2 *l2 = reinterpret_cast<__half2 *>(xl + (int64_t)row * kpad);
-  for (int k = 2 * threadIdx.x; k < kpad; k += 2 * blockDim.x) {
+  __half2 *h2 = reinterpret_cast<__half2 *>(x2 + (int64_t)row * kpad);
+  __half2 *l2 = reinterpret_cast<__half2 *>(x2 + (int64_t)(bn + row) * kpad);
+  for (int p = threadIdx.x; p < kpad / 2; p += blockDim.x) {  // p: fp16 pair = TMEM column c of block p / 16
+    const int c = p & 15, k = (p >> 4) * 32 + 8 * (c & 3) + 2 * (c >> 2);
     const float v0 = (live && k < K) ? xr[k] * sc : 0.0f, v1 = (live && k + 1 < K) ? xr[k + 1] * sc : 0.0f;
     const __half2 hh = __floats2half2_rn(v0, v1);
     const float2 hf = __half22float2(hh);
-    h2[k >> 1] = hh;
-    l2[k >> 1] = __floats2half2_rn(v0 - hf.x, v1 - hf.y);
+    h2[p] = hh;
+    l2[p] = __floats2half2_rn(v0 - hf.x, v1 - hf.y);
   }
   if (want_sums) {
     const int nb = kpad >> 5;

@@ -18,7 +18,7 @@ struct DecPlan {
 
 // Scratch one launch pair needs.
 struct DecBuffers {
-  __half *xh, *xl;    // [bn][kpad] each: activation rows split into fp16 hi + lo
+  __half *x2;         // [2 bn][kpad]: activation rows split into fp16 hi rows, then lo rows
   float *xsum;        // [kpad / 32][bn]: scaled block sums of x (Q4_1)
   float *xinv;        // [bn]: 2^-e per activation row
   float *partial;     // [grid][2][128][bn]: head / tail partial tile of every CTA
@@ -29,9 +29,12 @@ struct DecBuffers {
 // max_grid caps the persistent grid (0: one CTA per SM).
 DecPlan tcdec_plan(const WeightView &w, int device, int max_grid = 0);
 
-// One launch pair (activation split + decode GEMM) for m <= 32 rows; bn is 16
-// for m <= 16, else 32. nan_on_abort: a timed-out bounded wait writes NaN to
-// the outputs instead of leaving them unwritten.
+inline int dec_tile_rows(int m) { return m <= 8 ? 8 : (m <= 16 ? 16 : 32); }
+
+// One launch pair (activation split + decode GEMM) for m <= 32 rows; bn (the
+// activation tile height, dec_tile_rows) is 8 for m <= 8, 16 for m <= 16, else
+// 32. nan_on_abort: a timed-out bounded wait writes NaN to the outputs instead
+// of leaving them unwritten.
 int tcdec_launch(const WeightView &w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
                  cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort);
 
