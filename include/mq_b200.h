@@ -105,7 +105,7 @@ int mq_weight_export(const mq_weight *w, void *dst, size_t dst_bytes);
 /* y[i, n] = sum_k x[i, k] * W[n, k] (+ bias[n]) for i in [0, m).
  * x: device F32 [m, ldx] with ldx >= cols; y: device F32 [m, ldy] with
  * ldy >= rows; bias: device F32 [rows] or NULL. Small m runs a streaming
- * GEMV, large m the tcgen05 tensor-core GEMM (see mq_set_path). The tensor-
+ * GEMV, larger m the tcgen05 tensor-core GEMMs (see mq_set_path). The tensor-
  * core paths keep per-(device, stream) scratch for the split activations,
  * allocated on first use and grown as needed (the growth synchronizes the
  * stream). A bounded wait that runs out inside a GEMM launch is reported as
@@ -144,11 +144,11 @@ int mq_linear_noalloc(const mq_weight *w, const float *x, int m, int ldx, const 
                       void *stream);
 
 /* Kernel selection for the next mq_linear calls on this thread:
- * 0 = automatic (default): SIMT GEMV for m == 1, tcgen05 decode GEMM for
- *     m <= 32, tcgen05 prefill GEMM above;
- * 1 = force the SIMT streaming GEMV, 2 = force the tcgen05 prefill GEMM,
- * 3 = force the mma.sync tensor-core GEMV, 4 = force the tcgen05 decode GEMM.
- * Returns the previous mode. */
+ * 0 = automatic (default): the stream-K SIMT GEMV for m <= 4, the tcgen05
+ *     decode GEMM for m <= 32, the tcgen05 prefill GEMM above;
+ * 1 = force the stream-K SIMT GEMV, 2 = force the tcgen05 prefill GEMM,
+ * 4 = force the tcgen05 decode GEMM (3 is not a mode; other values are
+ * ignored). Returns the previous mode. */
 int mq_set_path(int mode);
 
 /* Number of kernels this library has launched in this process (all devices,

@@ -13,9 +13,7 @@
 
 #include "mq_common.cuh"
 #include "mq_gemm.cuh"
-#include "mq_gemv.cuh"
 #include "mq_pack.cuh"
-#include "mq_tcgemv.cuh"
 
 namespace mq {
 
@@ -43,11 +41,9 @@ void count_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_r
 
 namespace {
 
-thread_local int g_path_mode = 0;  // 0 auto, 1 GEMV, 2 GEMM
+thread_local int g_path_mode = 0;  // see mq_set_path in mq_b200.h
 
 bool valid_qtype(int q) { return q == MQ_Q8_0 || q == MQ_Q4_0 || q == MQ_Q4_1; }
-
-size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Switches the calling thread to `device` for the scope and restores it.
 struct DeviceGuard {
@@ -62,69 +58,6 @@ struct DeviceGuard {
     if (prev >= 0) cudaSetDevice(prev);
   }
 };
-
-int env_int(const char *name, int dflt) {
-  const char *v = std::getenv(name);
-  return v && *v ? std::atoi(v) : dflt;
-}
-
-int sm_count(int device) {
-  static std::mutex mu;
-  static std::vector<int> cache;
-  std::lock_guard<std::mutex> lock(mu);
-  if ((int)cache.size() <= device) cache.resize(device + 1, 0);
-  if (!cache[device]) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0) n = 148;
-    cache[device] = n;
-  }
-  return cache[device];
-}
-
-// ---------------------------------------------------------------------------
-// SIMT GEMV launch: M activation rows (1 or 2 per launch), RPW rows per warp.
-// A CTA has 8 warps: warps_k split the K groups, warps_r = 8 / warps_k own
-// different rows.
-// ---------------------------------------------------------------------------
-template <int QT, int M, int RPW>
-cudaError_t launch_gemv_t(const GemvArgs &a, int warps_k, cudaStream_t s) {
-  const int warps_r = 8 / warps_k;
-  const int rows_per_cta = RPW * warps_r;
-  const int grid = (a.w.rows + rows_per_cta - 1) / rows_per_cta;
-  gemv_kernel<QT, M, RPW><<<grid, 256, 0, s>>>(a, warps_k);
-  count_launch();
-  return cudaGetLastError();
-}
-
-template <int QT>
-cudaError_t launch_gemv_q(const GemvArgs &a, int m, int warps_k, cudaStream_t s) {
-  if (m == 1) return launch_gemv_t<QT, 1, 2>(a, warps_k, s);
-  return launch_gemv_t<QT, 2, 2>(a, warps_k, s);
-}
-
-}  // namespace
-
-int run_gemv(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-             cudaStream_t s) {
-  // K split: enough warps that each lane owns about one 4-block group.
-  int warps_k = env_int("MQ_GEMV_WARPS_K", 0);
-  if (warps_k <= 0) warps_k = std::min(8, std::max(1, (w->v.nb4 + 31) / 32));
-  warps_k = warps_k >= 8 ? 8 : warps_k >= 4 ? 4 : warps_k >= 2 ? 2 : 1;
-  for (int i0 = 0; i0 < m; i0 += 2) {
-    const int mm = std::min(2, m - i0);
-    GemvArgs a{w->v, x + (int64_t)i0 * ldx, ldx, bias, y + (int64_t)i0 * ldy, ldy};
-    cudaError_t e;
-    switch (w->v.qtype) {
-    case MQ_Q8_0: e = launch_gemv_q<MQ_Q8_0>(a, mm, warps_k, s); break;
-    case MQ_Q4_0: e = launch_gemv_q<MQ_Q4_0>(a, mm, warps_k, s); break;
-    default: e = launch_gemv_q<MQ_Q4_1>(a, mm, warps_k, s); break;
-    }
-    if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
-  }
-  return MQ_OK;
-}
-
-namespace {
 
 // Maps a QuantFail to the ABI code and the reference's exception message
 // (src/quantized_tensor.cc:119-120, 134-135, 140-141).
@@ -168,11 +101,6 @@ int quantize_host(int qtype, const float *src, int rows, int cols, uint8_t *dst,
   for (int t = 0; t < threads; ++t)
     if (first_bad[t] < best) best = first_bad[t], rc = code[t];
   return quant_status(rc);
-}
-
-Planes planes_of(const mq_weight *w) {
-  return Planes{const_cast<uint8_t *>(w->v.qs), reinterpret_cast<uint16_t *>(const_cast<__half *>(w->v.d)),
-                reinterpret_cast<uint16_t *>(const_cast<__half *>(w->v.mn)), w->v.ld_qs, w->v.ld_s};
 }
 
 }  // namespace
@@ -278,12 +206,8 @@ int mq_weight_shard_create(int device, int qtype, int rows, int cols, int row_be
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
   const int nrows = row_end - row_begin, nb = (cols + 31) / 32, bb = block_bytes(qtype);
-  const int nb4 = (nb + 3) / 4, rows_pad = (nrows + 15) / 16 * 16;
-  const int64_t ld_qs = (int64_t)nb4 * group_bytes(qtype);   // multiple of 64 bytes
-  const int64_t ld_s = (int64_t)round_up(4 * nb4, 8);       // 16-byte aligned scale rows
-  const size_t qs_bytes = round_up((size_t)rows_pad * ld_qs, 256);
-  const size_t s_bytes = round_up((size_t)rows_pad * ld_s * 2, 256);
-  const size_t total = qs_bytes + s_bytes * (qtype == MQ_Q4_1 ? 2 : 1);
+  const int steps = (nb + kStepBlocks - 1) / kStepBlocks, tiles = (nrows + kTileRows - 1) / kTileRows;
+  const size_t total = (size_t)tiles * steps * (size_t)step_chunk_bytes(qtype);
 
   auto *w = new (std::nothrow) mq_weight;
   if (!w) return fail(MQ_ERR_INVALID, "out of host memory");
@@ -297,9 +221,8 @@ int mq_weight_shard_create(int device, int qtype, int rows, int cols, int row_be
   }
   w->bytes = total;
   uint8_t *base = static_cast<uint8_t *>(w->base);
-  w->v = WeightView{qtype, nrows, cols, nb, nb4, rows_pad, base, reinterpret_cast<const __half *>(base + qs_bytes),
-                    qtype == MQ_Q4_1 ? reinterpret_cast<const __half *>(base + qs_bytes + s_bytes) : nullptr,
-                    ld_qs, ld_s};
+  w->v = WeightView{qtype, nrows, cols, nb, steps, tiles, tiles * kTileRows, base, step_chunk_bytes(qtype),
+                    step_pk_bytes(qtype)};
   const size_t shard_src_bytes = (size_t)nrows * nb * bb;
   const uint8_t *src = static_cast<const uint8_t *>(blocks) + (size_t)row_begin * nb * bb;
   void *staging = nullptr;
@@ -311,7 +234,7 @@ int mq_weight_shard_create(int device, int qtype, int rows, int cols, int row_be
   }
   if (e == cudaSuccess) {
     const int64_t n = (int64_t)nrows * nb;
-    repack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(src, qtype, nrows, nb, planes_of(w));
+    repack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(src, w->v);
     count_launch();
     e = cudaGetLastError();
   }
@@ -359,8 +282,7 @@ int mq_weight_export(const mq_weight *w, void *dst, size_t dst_bytes) {
   void *tmp = nullptr;
   MQ_CUDA(cudaMalloc(&tmp, need));
   const int64_t n = (int64_t)w->v.rows * w->v.nb;
-  unpack_kernel<<<(unsigned)((n + 255) / 256), 256>>>(static_cast<uint8_t *>(tmp), w->v.qtype, w->v.rows, w->v.nb,
-                                                      planes_of(w));
+  unpack_kernel<<<(unsigned)((n + 255) / 256), 256>>>(static_cast<uint8_t *>(tmp), w->v);
   count_launch();
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) e = cudaMemcpy(dst, tmp, need, cudaMemcpyDeviceToHost);
@@ -371,7 +293,7 @@ int mq_weight_export(const mq_weight *w, void *dst, size_t dst_bytes) {
 
 int mq_set_path(int mode) {
   const int prev = g_path_mode;
-  if (mode >= 0 && mode <= 4) g_path_mode = mode;
+  if (mode == 0 || mode == 1 || mode == 2 || mode == 4) g_path_mode = mode;
   return prev;
 }
 
@@ -388,15 +310,12 @@ int mq_linear(const mq_weight *w, const float *x, int m, int ldx, const float *b
   if (g.err != cudaSuccess) return cuda_fail(g.err, "cudaSetDevice");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int mode = g_path_mode;
-  if (mode == 1) return run_gemv(w, x, m, ldx, bias, y, ldy, s);
-  if (mode == 3) return run_tcgemv(w, x, m, ldx, bias, y, ldy, s);
+  if (!gemm_supported(w->device))
+    return fail(MQ_ERR_UNSUPPORTED, "the kernels need an sm_100 device (device %d)", w->device);
+  if (mode == 1) return run_sdec(w, x, m, ldx, bias, y, ldy, s);
   if (mode == 4) return run_tcdec(w, x, m, ldx, bias, y, ldy, s);
-  if (mode == 2 || (mode == 0 && m > tcgemv_max_m())) {
-    if (!gemm_supported(w->device))
-      return fail(MQ_ERR_UNSUPPORTED, "the tensor-core GEMM needs an sm_100 device (device %d)", w->device);
-    return run_gemm(w, x, m, ldx, bias, y, ldy, s);
-  }
-  if (m <= simt_max_m()) return run_gemv(w, x, m, ldx, bias, y, ldy, s);
+  if (mode == 2 || (mode == 0 && m > decode_max_m())) return run_gemm(w, x, m, ldx, bias, y, ldy, s);
+  if (m <= sdec_max_m()) return run_sdec(w, x, m, ldx, bias, y, ldy, s);
   return run_tcdec(w, x, m, ldx, bias, y, ldy, s);
 }
 

@@ -39,40 +39,64 @@ __host__ __device__ inline int block_bytes(int qtype) {
 __host__ __device__ inline int block_qbytes(int qtype) { return qtype == MQ_Q8_0 ? 32 : 16; }
 
 // ---------------------------------------------------------------------------
-// Device-resident weight ("lane-permuted rows").
+// Device-resident weight ("step chunks").
 //
-// The GGUF block interleave (2-byte aligned 34/18/20-byte blocks) is split
-// into planes, and the quant bytes of every row are grouped by 4 blocks and
-// permuted so that one aligned 16-byte load hands each consumer exactly the
-// nibbles/bytes it decodes:
-//   qs : [rows_pad][ld_qs] bytes; block group G (blocks 4G..4G+3) of a row
-//        occupies 64 bytes (Q4_x) or 128 bytes (Q8_0) at G * group bytes.
-//        Q4_x: byte 16*t + 4*j + p = quant byte 2t + {0, 8, 1, 9}[p] of block j;
-//        Q8_0: byte 32*t + 8*j + p = quant byte 2t + {0,1,8,9,16,17,24,25}[p].
-//        For t = 0..3 these are the K positions {2t, 2t+1, 2t+8, 2t+9} (+16)
-//        an mma.m16n8k16 fragment lane with threadID_in_group t holds.
-//   d  : [rows_pad][ld_s] fp16 scales;  mn : [rows_pad][ld_s] fp16 Q4_1 mins.
-// Rows are padded to a multiple of 16 and blocks to a multiple of 4 with
-// zero bytes (a zero scale decodes to 0), so tile loops need no bounds
-// checks on loads. Apart from that padding the bytes per weight are the GGUF
-// ones.
+// The kernels stream a weight as a sequence of (tile, step) units: a tile is
+// 128 rows, a step 8 quant blocks (256 K). Each unit is one contiguous chunk,
+// tile-major, so that a persistent CTA walking consecutive units reads one
+// contiguous address range with a single bulk copy per unit:
+//   chunk(t, k) = base + (t * steps + k) * chunk_bytes
+//   [ packed quant bytes | fp16 scales d [128][8] | fp16 Q4_1 mins [128][8] ]
+// Packed bytes: Q4_x 128 rows x 128 B; Q8_0 two halves of 128 rows x 128 B
+// (half = quad). A quad is 4 blocks; inside a row's quad the bytes follow
+//   Q4_x: byte 16*t + 4*j + p = quant byte 2t + {0, 8, 1, 9}[p] of block j;
+//   Q8_0: byte 32*t + 8*j + p = quant byte 2t + {0,1,8,9,16,17,24,25}[p],
+// i.e. the K positions {2t, 2t+1, 2t+8, 2t+9} (+16) that one 16-byte chunk
+// (Q4_x) or 32-byte pair of chunks (Q8_0) hands each consumer, and every
+// 128-byte row is stored with the 16-byte chunk c at position c ^ (row & 7)
+// (the 128-byte swizzle of a TMA tile, pre-applied, so that the threads that
+// read one chunk position of 32 consecutive rows hit distinct banks).
+// Rows are padded to a multiple of 128 and blocks to a multiple of 8 with
+// zero bytes (a zero scale decodes to 0), so no kernel needs bounds checks on
+// weight loads. Apart from that padding the bytes per weight are the GGUF ones.
 // ---------------------------------------------------------------------------
+constexpr int kTileRows = 128;
+constexpr int kStepBlocks = 8;
+
 struct WeightView {
   int qtype, rows, cols, nb;   // nb = ceil(cols / 32)
-  int nb4, rows_pad;           // ceil(nb / 4), rows rounded up to 16
-  const uint8_t *qs;
-  const __half *d, *mn;
-  int64_t ld_qs;               // bytes per row of qs (nb4 * group bytes)
-  int64_t ld_s;                // halves per row of d / mn
+  int steps, tiles, rows_pad;  // ceil(nb / 8), rows_pad / 128, rows rounded up to 128
+  const uint8_t *base;         // chunk(0, 0)
+  int64_t chunk_bytes;         // bytes of one (tile, step) chunk
+  int pk_bytes;                // packed quant bytes at the start of a chunk
 };
 
-__host__ __device__ inline int group_bytes(int qtype) { return qtype == MQ_Q8_0 ? 128 : 64; }
+__host__ __device__ constexpr int group_bytes(int qtype) { return qtype == MQ_Q8_0 ? 128 : 64; }
+__host__ __device__ constexpr int step_pk_bytes(int qtype) { return kTileRows * (qtype == MQ_Q8_0 ? 256 : 128); }
+__host__ __device__ constexpr int step_sc_bytes(int qtype) { return kTileRows * 16 * (qtype == MQ_Q4_1 ? 2 : 1); }
+__host__ __device__ constexpr int64_t step_chunk_bytes(int qtype) { return step_pk_bytes(qtype) + step_sc_bytes(qtype); }
 
-// Position, inside its 4-block group, of quant byte i of block j.
+// Position, inside its 4-block group (quad), of quant byte i of block j.
 __host__ __device__ inline int permuted_pos(int qtype, int i, int j) {
   const int t = (i & 7) >> 1;
   if (qtype == MQ_Q8_0) return 32 * t + 8 * j + 2 * (i >> 3) + (i & 1);
   return 16 * t + 4 * j + ((i >> 3) | ((i & 1) << 1));
+}
+
+// Byte offset, inside a chunk, of 16-byte chunk c (0..7) of tile row r in
+// half h (Q8_0; 0 for Q4_x).
+__host__ __device__ inline int chunk16_off(int r, int c, int h) { return h * (kTileRows * 128) + r * 128 + ((c ^ (r & 7)) << 4); }
+
+// Byte offset, inside a chunk, of quant byte i of step block jb (0..7) of tile row r.
+__host__ __device__ inline int pk_byte_off(int qtype, int r, int jb, int i) {
+  const int pos = permuted_pos(qtype, i, jb & 3);
+  if (qtype == MQ_Q8_0) return chunk16_off(r, pos >> 4, jb >> 2) + (pos & 15);
+  return chunk16_off(r, 4 * (jb >> 2) + (pos >> 4), 0) + (pos & 15);
+}
+
+// Chunk of (tile t, step k); scales of row r at + pk_bytes + 16 r, mins at + pk_bytes + 2048 + 16 r.
+__host__ __device__ inline const uint8_t *chunk_ptr(const WeightView &w, int t, int k) {
+  return w.base + ((int64_t)t * w.steps + k) * w.chunk_bytes;
 }
 
 // ---------------------------------------------------------------------------

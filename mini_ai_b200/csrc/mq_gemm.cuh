@@ -214,27 +214,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int n = n0 + r;
     const bool row_ok = n < a.w.rows;
     const WeightView &w = a.w;
-    const uint8_t *qrow = w.qs + (int64_t)(row_ok ? n : 0) * w.ld_qs;
-    const __half *drow = w.d + (int64_t)(row_ok ? n : 0) * w.ld_s;
-    const __half *mrow = QT == MQ_Q4_1 ? w.mn + (int64_t)(row_ok ? n : 0) * w.ld_s : nullptr;
+    const int rn = row_ok ? n : 0, tn = rn / kTileRows, rr = rn % kTileRows;
 
     StepWords<QT> qn;
     float2 dn = make_float2(0.0f, 0.0f), mnn = make_float2(0.0f, 0.0f);
     auto fetch = [&](int kt) {  // blocks 2kt, 2kt+1 (zero-padded past nb in the layout)
-      const uint8_t *grp = qrow + (int64_t)(kt >> 1) * group_bytes(QT) + 8 * (kt & 1) * (QT == MQ_Q8_0 ? 2 : 1);
+      const uint8_t *chunk = chunk_ptr(w, tn, kt >> 2);  // 8 blocks per chunk step
+      const int qd = (kt & 3) >> 1, jb = 2 * (kt & 3);    // quad of the step, first block of the pair
       if (row_ok) {
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           if constexpr (QT == MQ_Q8_0) {
-            const uint4 v = ld_stream_v4(grp + 32 * t);
+            const uint4 v = ld_stream_v4(chunk + chunk16_off(rr, 2 * t + (kt & 1), qd));
             qn.w[t][0][0] = v.x, qn.w[t][0][1] = v.y, qn.w[t][1][0] = v.z, qn.w[t][1][1] = v.w;
           } else {
-            const uint2 v = ld_stream_v2(grp + 16 * t);
+            const uint2 v = ld_stream_v2(chunk + chunk16_off(rr, 4 * qd + t, 0) + 8 * (kt & 1));
             qn.w[t][0][0] = v.x, qn.w[t][1][0] = v.y;
           }
         }
-        dn = __half22float2(*reinterpret_cast<const __half2 *>(drow + 2 * kt));
-        if constexpr (QT == MQ_Q4_1) mnn = __half22float2(*reinterpret_cast<const __half2 *>(mrow + 2 * kt));
+        const uint8_t *sc = chunk + w.pk_bytes + rr * 16 + 2 * jb;
+        dn = __half22float2(*reinterpret_cast<const __half2 *>(sc));
+        if constexpr (QT == MQ_Q4_1) mnn = __half22float2(*reinterpret_cast<const __half2 *>(sc + 2048));
       } else {
 #pragma unroll
         for (int t = 0; t < 4; ++t)
@@ -303,15 +303,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // Host side (mq_gemm_host.cuh).
-int simt_max_m();
-int tcgemv_max_m();
+int decode_max_m();
+int sdec_max_m();
 bool gemm_supported(int device);
-int run_tcgemv(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-               cudaStream_t s);
+int run_sdec(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
+             cudaStream_t s);
 int run_tcdec(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
               cudaStream_t s);
 int run_gemm(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
              cudaStream_t s);
-int run_gemv(const mq_weight *, const float *, int, int64_t, const float *, float *, int64_t, cudaStream_t);
 
 }  // namespace mq

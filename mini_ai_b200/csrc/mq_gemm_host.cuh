@@ -9,8 +9,8 @@
 #include <utility>
 
 #include "mq_gemm.cuh"
+#include "mq_sdec.cuh"
 #include "mq_tcdec.cuh"
-#include "mq_tcgemv.cuh"
 
 namespace mq {
 
@@ -144,8 +144,7 @@ int make_tmap(CUtensorMap *map, CUtensorMapDataType dtype, int elem, const void 
 }
 
 template <int QT, int BN, int NC>
-cudaError_t launch_tcdec_t(const CUtensorMap &tq, const CUtensorMap &td, const CUtensorMap &tm, const CUtensorMap &tx,
-                           const DecArgs &a, int grid, cudaStream_t s) {
+cudaError_t launch_tcdec_t(const CUtensorMap &tx, const DecArgs &a, int grid, cudaStream_t s) {
   using L = DecCfg<QT, BN>;
   static bool configured = false;
   if (!configured) {
@@ -153,18 +152,17 @@ cudaError_t launch_tcdec_t(const CUtensorMap &tq, const CUtensorMap &td, const C
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  tcdec_kernel<QT, BN, NC><<<grid, kDecThreads, L::kAlloc, s>>>(tq, td, tm, tx, a);
+  tcdec_kernel<QT, BN, NC><<<grid, kDecThreads, L::kAlloc, s>>>(tx, a);
   count_launch();
   return cudaGetLastError();
 }
 
 template <int QT>
-cudaError_t launch_tcdec_q(const CUtensorMap &tq, const CUtensorMap &td, const CUtensorMap &tm, const CUtensorMap &tx,
-                           const DecArgs &a, int grid, int m, cudaStream_t s) {
-  if (m <= 4) return launch_tcdec_t<QT, 8, 4>(tq, td, tm, tx, a, grid, s);
-  if (m <= 8) return launch_tcdec_t<QT, 8, 8>(tq, td, tm, tx, a, grid, s);
-  if (m <= 16) return launch_tcdec_t<QT, 16, 16>(tq, td, tm, tx, a, grid, s);
-  return launch_tcdec_t<QT, 32, 32>(tq, td, tm, tx, a, grid, s);
+cudaError_t launch_tcdec_q(const CUtensorMap &tx, const DecArgs &a, int grid, int m, cudaStream_t s) {
+  if (m <= 4) return launch_tcdec_t<QT, 8, 4>(tx, a, grid, s);
+  if (m <= 8) return launch_tcdec_t<QT, 8, 8>(tx, a, grid, s);
+  if (m <= 16) return launch_tcdec_t<QT, 16, 16>(tx, a, grid, s);
+  return launch_tcdec_t<QT, 32, 32>(tx, a, grid, s);
 }
 
 template <int QT, int BN, int STAGES>
@@ -190,16 +188,10 @@ int env_threshold(const char *name, int dflt) {
   return e && *e ? std::atoi(e) : dflt;
 }
 
-// Largest activation count served by the SIMT GEMV in automatic mode.
-int simt_max_m() {
-  static const int v = env_threshold("MQ_SIMT_MAX_M", 1);
-  return v;
-}
-
-// Largest activation count served by the tensor-core GEMV; above it the
-// tcgen05 GEMM takes over.
-int tcgemv_max_m() {
-  static const int v = std::min(32, env_threshold("MQ_TCGEMV_MAX_M", 32));
+// Largest activation count served by the decode kernels in automatic mode;
+// above it the tcgen05 prefill GEMM takes over.
+int decode_max_m() {
+  static const int v = std::min(32, env_threshold("MQ_DECODE_MAX_M", 32));
   return v;
 }
 
@@ -210,77 +202,11 @@ bool gemm_supported(int device) {
   return major == 10 && minor == 0;
 }
 
-namespace {
-template <int QT, int NT, int RG>
-cudaError_t launch_tcgemv_t(const TcArgs &a, cudaStream_t s) {
-  constexpr int kWarps = 8;
-  constexpr int smem = kWarps * RG * NT * 4 * 32 * (int)sizeof(float);
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(tcgemv_kernel<QT, NT, RG>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
-  const int grid = (a.w.rows_pad + 16 * RG - 1) / (16 * RG);
-  tcgemv_kernel<QT, NT, RG><<<grid, kWarps * 32, smem, s>>>(a);
-  count_launch();
-  return cudaGetLastError();
-}
-
-template <int QT, int NT>
-cudaError_t launch_tcgemv_n(const TcArgs &a, int rg, cudaStream_t s) {
-  if (rg >= 4 && NT < 4) return launch_tcgemv_t<QT, NT, (NT < 4 ? 4 : 2)>(a, s);  // NT = 4 caps RG at 2 (registers)
-  if (rg >= 2) return launch_tcgemv_t<QT, NT, 2>(a, s);
-  return launch_tcgemv_t<QT, NT, 1>(a, s);
-}
-
-template <int QT>
-cudaError_t launch_tcgemv_q(const TcArgs &a, int nt, int rg, cudaStream_t s) {
-  if (nt == 1) return launch_tcgemv_n<QT, 1>(a, rg, s);
-  if (nt == 2) return launch_tcgemv_n<QT, 2>(a, rg, s);
-  return launch_tcgemv_n<QT, 4>(a, rg, s);
-}
-}  // namespace
-
-// Tensor-core GEMV: up to 32 activation rows per launch (split + kernel).
-int run_tcgemv(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-               cudaStream_t s) {
-  const WeightView &w = wt->v;
-  const int nbp = 4 * w.nb4;
-  const int sms = 148;
-  for (int i0 = 0; i0 < m; i0 += 32) {
-    const int mm = std::min(32, m - i0);
-    const int nt = mm <= 8 ? 1 : mm <= 16 ? 2 : 4;
-    const size_t xf_bytes = (size_t)nt * nbp * 2 * 32 * 16, xs_bytes = (size_t)nt * nbp * 8 * 4;
-    void *ws = nullptr;
-    int rc = workspace_for(wt->device, s, xf_bytes + xs_bytes + 8 * nt * 4 + 256, &ws);
-    if (rc) return rc;
-    uint4 *xf = static_cast<uint4 *>(ws);
-    float *xsum = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + xf_bytes);
-    float *xinv = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + xf_bytes + xs_bytes);
-    tcx_prep_kernel<<<8 * nt, 256, 0, s>>>(x + (int64_t)i0 * ldx, ldx, mm, w.cols, nbp, xf, xsum, xinv,
-                                           w.qtype == MQ_Q4_1);
-    count_launch();
-    MQ_CUDA(cudaGetLastError());
-    int rg = env_threshold("MQ_TCGEMV_RG", 0);
-    if (rg <= 0) rg = (w.rows_pad / 64 >= 2 * sms) ? 4 : (w.rows_pad / 32 >= 2 * sms) ? 2 : 1;
-    TcArgs a{w, xf, xsum, xinv, mm, bias, y + (int64_t)i0 * ldy, ldy};
-    cudaError_t e;
-    switch (w.qtype) {
-    case MQ_Q8_0: e = launch_tcgemv_q<MQ_Q8_0>(a, nt, rg, s); break;
-    case MQ_Q4_0: e = launch_tcgemv_q<MQ_Q4_0>(a, nt, rg, s); break;
-    default: e = launch_tcgemv_q<MQ_Q4_1>(a, nt, rg, s); break;
-    }
-    if (e != cudaSuccess) return cuda_fail(e, "tensor-core gemv launch");
-  }
-  return MQ_OK;
-}
-
 DecPlan tcdec_plan(const WeightView &w, int device, int max_grid) {
   DecPlan p;
-  p.steps = (w.nb4 + 1) / 2;  // 8 blocks (two 4-block groups) per packed step
-  p.kpad = p.steps * kDecBlocksPerStep * 32;
-  p.tiles = (w.rows_pad + kDecRows - 1) / kDecRows;
+  p.steps = w.steps;
+  p.kpad = w.steps * kDecBlocksPerStep * 32;
+  p.tiles = w.tiles;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   int grid = env_threshold("MQ_TCDEC_GRID", 0);
@@ -297,25 +223,17 @@ int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const
                                       w.qtype == MQ_Q4_1);
   count_launch();
   MQ_CUDA(cudaGetLastError());
-  CUtensorMap tq, td, tm, tx;
+  CUtensorMap tx;
   int rc;
-  if ((rc = make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.qs, w.rows_pad, w.ld_qs, w.ld_qs, 128, kDecRows)))
-    return rc;
-  if ((rc = make_tmap(&td, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.d, w.rows_pad, w.ld_s, w.ld_s, kDecBlocksPerStep,
-                      kDecRows, CU_TENSOR_MAP_SWIZZLE_NONE)))
-    return rc;
-  if ((rc = make_tmap(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.qtype == MQ_Q4_1 ? w.mn : w.d, w.rows_pad, w.ld_s,
-                      w.ld_s, kDecBlocksPerStep, kDecRows, CU_TENSOR_MAP_SWIZZLE_NONE)))
-    return rc;
   if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf.x2, 2 * bn, plan.kpad, plan.kpad, 64, 2 * bn)))
     return rc;
   DecArgs a{w, mm, buf.xinv, buf.xsum, bias, y, ldy, buf.partial, buf.tickets, plan.steps, plan.tiles, buf.err,
             nan_on_abort};
   cudaError_t e;
   switch (w.qtype) {
-  case MQ_Q8_0: e = launch_tcdec_q<MQ_Q8_0>(tq, td, tm, tx, a, plan.grid, mm, s); break;
-  case MQ_Q4_0: e = launch_tcdec_q<MQ_Q4_0>(tq, td, tm, tx, a, plan.grid, mm, s); break;
-  default: e = launch_tcdec_q<MQ_Q4_1>(tq, td, tm, tx, a, plan.grid, mm, s); break;
+  case MQ_Q8_0: e = launch_tcdec_q<MQ_Q8_0>(tx, a, plan.grid, mm, s); break;
+  case MQ_Q4_0: e = launch_tcdec_q<MQ_Q4_0>(tx, a, plan.grid, mm, s); break;
+  default: e = launch_tcdec_q<MQ_Q4_1>(tx, a, plan.grid, mm, s); break;
   }
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 decode launch");
   return MQ_OK;
@@ -353,6 +271,89 @@ int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
     buf.err = err_dev;
     if ((rc = tcdec_launch(w, x + (int64_t)i0 * ldx, mm, ldx, bias, y + (int64_t)i0 * ldy, ldy, s, plan, buf, 0)))
       return rc;
+  }
+  return MQ_OK;
+}
+
+namespace {
+
+template <int QT, int MC>
+cudaError_t launch_sdec_t(const CUtensorMap &tx, const SdecArgs &a, int grid, cudaStream_t s) {
+  using L = SdCfg<QT, MC>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(sdec_kernel<QT, MC>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  sdec_kernel<QT, MC><<<grid, kSdThreads, L::kAlloc, s>>>(tx, a);
+  count_launch();
+  return cudaGetLastError();
+}
+
+template <int QT>
+cudaError_t launch_sdec_q(const CUtensorMap &tx, const SdecArgs &a, int grid, int mc, cudaStream_t s) {
+  if (mc == 1) return launch_sdec_t<QT, 1>(tx, a, grid, s);
+  if (mc == 2) return launch_sdec_t<QT, 2>(tx, a, grid, s);
+  return launch_sdec_t<QT, 4>(tx, a, grid, s);
+}
+
+}  // namespace
+
+// Largest activation count served by the stream-K SIMT GEMV (mq_sdec.cuh).
+int sdec_max_m() {
+  static const int v = env_threshold("MQ_SDEC_MAX_M", 4);
+  return v;
+}
+
+// Stream-K SIMT GEMV: up to 4 activation rows per launch. The activations
+// are read by TMA straight from x when its base and row stride are 16-byte
+// aligned; otherwise they are first copied to an aligned scratch.
+int run_sdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
+             cudaStream_t s) {
+  int *err_dev = nullptr, *err_host = nullptr;
+  int rc = err_flag(wt->device, &err_dev, &err_host);
+  if (rc) return rc;
+  if (*(volatile int *)err_host) {
+    *(volatile int *)err_host = 0;
+    return fail(MQ_ERR_TIMEOUT, "an earlier stream-K launch on device %d ran out of a bounded wait", wt->device);
+  }
+  const WeightView &w = wt->v;
+  const DecPlan plan = tcdec_plan(w, wt->device);
+  int *tickets = nullptr;
+  if ((rc = tickets_for(wt->device, s, (size_t)plan.tiles, &tickets))) return rc;
+  for (int i0 = 0; i0 < m; i0 += 4) {
+    const int mm = std::min(4, m - i0);
+    const int mc = mm == 1 ? 1 : (mm == 2 ? 2 : 4);
+    const float *xs = x + (int64_t)i0 * ldx;
+    int64_t ldxs = ldx;
+    const bool copy = (reinterpret_cast<uintptr_t>(xs) & 15) != 0 || (ldx & 3) != 0;
+    const int64_t ldc = ((int64_t)w.cols + 3) & ~int64_t(3);
+    const size_t pbytes = (size_t)plan.grid * 2 * kSdRows * mc * 4;
+    const size_t cbytes = copy ? (size_t)mm * ldc * 4 : 0;
+    void *ws = nullptr;
+    if ((rc = workspace_for(wt->device, s, pbytes + cbytes + 1024, &ws))) return rc;
+    uint8_t *base = static_cast<uint8_t *>(ws);
+    if (copy) {
+      float *xc = reinterpret_cast<float *>(base + ((pbytes + 255) & ~size_t(255)));
+      MQ_CUDA(cudaMemcpy2DAsync(xc, (size_t)ldc * 4, xs, (size_t)ldx * 4, (size_t)w.cols * 4, (size_t)mm,
+                                cudaMemcpyDeviceToDevice, s));
+      xs = xc;
+      ldxs = ldc;
+    }
+    CUtensorMap tx;
+    if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xs, mm, w.cols, ldxs, 256, mc,
+                        CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return rc;
+    SdecArgs a{w, mm, bias, y + (int64_t)i0 * ldy, ldy, reinterpret_cast<float *>(base), tickets, plan.steps,
+               plan.tiles, err_dev, 0};
+    cudaError_t e;
+    switch (w.qtype) {
+    case MQ_Q8_0: e = launch_sdec_q<MQ_Q8_0>(tx, a, plan.grid, mc, s); break;
+    case MQ_Q4_0: e = launch_sdec_q<MQ_Q4_0>(tx, a, plan.grid, mc, s); break;
+    default: e = launch_sdec_q<MQ_Q4_1>(tx, a, plan.grid, mc, s); break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "stream-K GEMV launch");
   }
   return MQ_OK;
 }

@@ -1,6 +1,6 @@
 // Weight layout kernels and the bit-exact block quantizer.
 //
-// * repack / unpack: GGUF block stream <-> the device planes of WeightView.
+// * repack / unpack: GGUF block stream <-> the step chunks of WeightView.
 // * quantize_block : one 32-slot block packed exactly as the reference's
 //   QuantizeTensor (src/quantized_tensor.cc:104-159) packs it. Shared by the
 //   host quantizer (threads over rows) and the device quantizer (one thread
@@ -13,44 +13,36 @@
 
 namespace mq {
 
-struct Planes {
-  uint8_t *qs;
-  uint16_t *d, *mn;
-  int64_t ld_qs, ld_s;
-};
-
-// GGUF block stream (rows x nb blocks, starting at `src`) -> device planes.
-__global__ void repack_kernel(const uint8_t *__restrict__ src, int qtype, int rows, int nb, Planes p) {
+// GGUF block stream (rows x nb blocks, starting at `src`) -> step chunks.
+__global__ void repack_kernel(const uint8_t *__restrict__ src, WeightView w) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (int64_t)rows * nb) return;
-  const int64_t r = i / nb;
-  const int b = (int)(i % nb);
-  const int bb = block_bytes(qtype), qb = block_qbytes(qtype), hdr = bb - qb;
+  if (i >= (int64_t)w.rows * w.nb) return;
+  const int r = (int)(i / w.nb), b = (int)(i % w.nb);
+  const int bb = block_bytes(w.qtype), qb = block_qbytes(w.qtype), hdr = bb - qb;
   const uint8_t *blk = src + i * bb;
-  p.d[r * p.ld_s + b] = (uint16_t)(blk[0] | (blk[1] << 8));
-  if (qtype == MQ_Q4_1) p.mn[r * p.ld_s + b] = (uint16_t)(blk[2] | (blk[3] << 8));
-  uint8_t *grp = p.qs + r * p.ld_qs + (int64_t)(b >> 2) * group_bytes(qtype);
-  for (int q = 0; q < qb; ++q) grp[permuted_pos(qtype, q, b & 3)] = blk[hdr + q];
+  const int rr = r % kTileRows, jb = b % kStepBlocks;
+  uint8_t *c = const_cast<uint8_t *>(chunk_ptr(w, r / kTileRows, b / kStepBlocks));
+  uint8_t *sc = c + w.pk_bytes + rr * 16 + 2 * jb;
+  sc[0] = blk[0];
+  sc[1] = blk[1];
+  if (w.qtype == MQ_Q4_1) sc[2048] = blk[2], sc[2049] = blk[3];
+  for (int q = 0; q < qb; ++q) c[pk_byte_off(w.qtype, rr, jb, q)] = blk[hdr + q];
 }
 
-// Device planes -> GGUF block stream (the inverse of repack_kernel).
-__global__ void unpack_kernel(uint8_t *__restrict__ dst, int qtype, int rows, int nb, const Planes p) {
+// Step chunks -> GGUF block stream (the inverse of repack_kernel).
+__global__ void unpack_kernel(uint8_t *__restrict__ dst, const WeightView w) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (int64_t)rows * nb) return;
-  const int64_t r = i / nb;
-  const int b = (int)(i % nb);
-  const int bb = block_bytes(qtype), qb = block_qbytes(qtype), hdr = bb - qb;
+  if (i >= (int64_t)w.rows * w.nb) return;
+  const int r = (int)(i / w.nb), b = (int)(i % w.nb);
+  const int bb = block_bytes(w.qtype), qb = block_qbytes(w.qtype), hdr = bb - qb;
   uint8_t *blk = dst + i * bb;
-  const uint16_t d = p.d[r * p.ld_s + b];
-  blk[0] = (uint8_t)(d & 255);
-  blk[1] = (uint8_t)(d >> 8);
-  if (qtype == MQ_Q4_1) {
-    const uint16_t m = p.mn[r * p.ld_s + b];
-    blk[2] = (uint8_t)(m & 255);
-    blk[3] = (uint8_t)(m >> 8);
-  }
-  const uint8_t *grp = p.qs + r * p.ld_qs + (int64_t)(b >> 2) * group_bytes(qtype);
-  for (int q = 0; q < qb; ++q) blk[hdr + q] = grp[permuted_pos(qtype, q, b & 3)];
+  const int rr = r % kTileRows, jb = b % kStepBlocks;
+  const uint8_t *c = chunk_ptr(w, r / kTileRows, b / kStepBlocks);
+  const uint8_t *sc = c + w.pk_bytes + rr * 16 + 2 * jb;
+  blk[0] = sc[0];
+  blk[1] = sc[1];
+  if (w.qtype == MQ_Q4_1) blk[2] = sc[2048], blk[3] = sc[2049];
+  for (int q = 0; q < qb; ++q) blk[hdr + q] = c[pk_byte_off(w.qtype, rr, jb, q)];
 }
 
 // Failure kinds of quantize_block (mapped to MQ_ERR_* and the reference's

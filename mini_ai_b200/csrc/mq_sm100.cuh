@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the GEMM uses:
-// mbarriers (bounded waits), TMA tile loads (no multicast), tcgen05 MMA with
+// mbarriers (bounded waits), TMA tile and bulk loads (no multicast), tcgen05 MMA with
 // TMEM accumulators, TMEM allocation and loads, and the UMMA descriptors.
 #pragma once
 
@@ -104,6 +104,13 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const void *tmap, in
           "r"(smem_u32(smem_dst)),
       "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
+}
+// Linear bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void *smem_dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");

@@ -45,8 +45,9 @@
 // Warp roles (16 warps; every role that blocks on an mbarrier has a warp of
 // its own, since a lane suspended in try_wait holds up the diverged lanes of
 // its warp):
-//   warp 0         TMA: packed quant rows (128-byte swizzle, PS stages) and
-//                  the fp16 block scales (+ Q4_1 mins) of each step (SS stages);
+//   warp 0         bulk copies of each step's weight chunk: packed quant rows
+//                  (pre-swizzled, PS stages) and fp16 block scales (+ Q4_1
+//                  mins, SS stages);
 //   warps 1, 3     TMEM allocation (warp 1); MMA issue from one thread each,
 //                  alternate quads, one commit per group;
 //   warp 2         TMA: fp16 activation tiles (hi rows, lo rows), one per quad;
@@ -111,6 +112,8 @@ struct DecCfg {
   static_assert(kDecGroupBars > (4 / G) * (NA - 1), "commit ring too short");
   static constexpr int kPkBytes = kDecRows * (QT == MQ_Q8_0 ? 256 : 128);  // packed step
   static constexpr int kScBytes = kDecRows * 16 * (QT == MQ_Q4_1 ? 2 : 1);  // scales (+ mins) of a step
+  static_assert(kDecRows == kTileRows && kPkBytes == step_pk_bytes(QT) && kScBytes == step_sc_bytes(QT),
+                "stages hold the parts of one weight chunk");
   static constexpr int kXBytes = N * 128 * 2;                               // activation tile of a quad (128 K)
   static constexpr int PS = QT == MQ_Q8_0 ? 3 : 4;  // packed stages
   static constexpr int SS = 6;                      // scale stages
@@ -211,9 +214,7 @@ __device__ __forceinline__ void tmem_ld_n(uint32_t taddr, uint32_t (&r)[N]) {
 
 template <int QT, int BN, int NC>
 __global__ void __launch_bounds__(kDecThreads, 1)
-    tcdec_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_d,
-                 const __grid_constant__ CUtensorMap tm_m, const __grid_constant__ CUtensorMap tm_x,
-                 const DecArgs a) {
+    tcdec_kernel(const __grid_constant__ CUtensorMap tm_x, const DecArgs a) {
   using L = DecCfg<QT, BN>;
   constexpr int PS = L::PS, SS = L::SS, XS = L::XS, NA = L::NA, ND = L::ND, G = L::G, N = L::N;
   constexpr int NGB = kDecGroupBars;
@@ -262,31 +263,21 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   auto quad_group = [&](int q) { return (4 * q + 3) / G; };
 
   if (warp == 0) {
-    if (lane == 0) {  // ------------------------------------- TMA: packed quant rows and their scales
-      sm100::prefetch_tmap(&tm_q);
-      sm100::prefetch_tmap(&tm_d);
-      if (QT == MQ_Q4_1) sm100::prefetch_tmap(&tm_m);
+    if (lane == 0) {  // ------------------------------------- bulk copies: packed quant rows and their scales
+      // A CTA's steps are consecutive chunks of the weight: one linear stream.
       int issued_pk = 0, issued_sc = 0;
       for (int ls = 0; ls < nsteps; ++ls) {
-        const int g = g0 + ls, t = g / S, k = g % S;
+        const int g = g0 + ls;
+        const uint8_t *chunk = chunk_ptr(a.w, g / S, g % S);
         const int i = ls % PS;
         if (!sm100::mbar_wait_sleep(&pk_empty[i], ((uint32_t)(ls / PS) & 1u) ^ 1u, a.err, abort, kDecWaitNs)) break;
-        uint8_t *dst = smem + L::kPkOff + i * L::kPkBytes;
         sm100::mbar_arrive_expect_tx(&pk_full[i], L::kPkBytes);
-        if constexpr (QT == MQ_Q8_0) {
-          sm100::tma_load_2d(dst, &tm_q, k * 256, t * kDecRows, &pk_full[i]);
-          sm100::tma_load_2d(dst + kDecRows * 128, &tm_q, k * 256 + 128, t * kDecRows, &pk_full[i]);
-        } else {
-          sm100::tma_load_2d(dst, &tm_q, k * 128, t * kDecRows, &pk_full[i]);
-        }
+        sm100::bulk_load(smem + L::kPkOff + i * L::kPkBytes, chunk, L::kPkBytes, &pk_full[i]);
         issued_pk = ls + 1;
         const int j = ls % SS;
         if (!sm100::mbar_wait_sleep(&sc_empty[j], ((uint32_t)(ls / SS) & 1u) ^ 1u, a.err, abort, kDecWaitNs)) break;
-        uint8_t *sdst = smem + L::kScOff + j * L::kScBytes;
         sm100::mbar_arrive_expect_tx(&sc_full[j], L::kScBytes);
-        sm100::tma_load_2d(sdst, &tm_d, k * kDecBlocksPerStep, t * kDecRows, &sc_full[j]);
-        if constexpr (QT == MQ_Q4_1)
-          sm100::tma_load_2d(sdst + kDecRows * 16, &tm_m, k * kDecBlocksPerStep, t * kDecRows, &sc_full[j]);
+        sm100::bulk_load(smem + L::kScOff + j * L::kScBytes, chunk + L::kPkBytes, L::kScBytes, &sc_full[j]);
         issued_sc = ls + 1;
       }
       for (int p = issued_pk - PS < 0 ? 0 : issued_pk - PS; p < issued_pk; ++p)

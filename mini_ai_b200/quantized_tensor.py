@@ -229,7 +229,8 @@ def CudaDeviceInfo() -> str:
 
 
 def set_path(mode: int) -> int:
-    """0 = automatic, 1 = force streaming GEMV, 2 = force tensor-core GEMM (this thread)."""
+    """Kernel selection for this thread (mq_set_path): 0 automatic, 1 stream-K SIMT GEMV,
+    2 tcgen05 prefill GEMM, 4 tcgen05 decode GEMM."""
     return lib().mq_set_path(mode)
 
 
