@@ -16,9 +16,13 @@ per product, over the whole step.
           activations from pinned host memory and its outputs back inside the
           timed region.
 
-Multi-GPU (torchrun): every rank serves its own independent decode batches
-with its own weight copy (replicas, weak scaling); value = all ranks' bytes /
-max-over-ranks time.
+Multi-GPU (torchrun, N ranks): tensor-parallel row sharding with weak
+scaling. Every matrix grows to N x its rows (an N-times wider FFN); rank r
+holds the equal row shard r, which is exactly the 1-GPU matrix size, so every
+GPU streams the same bytes as the 1-GPU run, and every product ends with the
+NCCL all-gather of the output slices over NVLink (mq_linear_sharded_allgather,
+inside the timed graph). value = all ranks' algorithmic bytes / max-over-ranks
+time.
 
 ``--impl reference`` times the reference's own CPU implementation
 (LinearDispatch kThreadedSimd from the reference sources built in
@@ -168,29 +172,40 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     sh = C.c_void_p(stream.cuda_stream)
 
     # Weights: generated on the device, packed by the bit-exact device quantizer.
+    # With N ranks each matrix has N x rows and this rank keeps row shard `rank`
+    # (the same seed on every rank, so the shards form one global matrix).
     gen = torch.Generator(device=dev)
     handles, host_blocks = [], []
     keep_host = rank == 0 and world == 1 and not args.no_cpu_baseline and not args.only
     for i, (q, m, name, n, k) in enumerate(prods):
-        gen.manual_seed(1000 * rank + i)
-        w32 = torch.randn((n, k), generator=gen, device=dev, dtype=torch.float32).mul_(0.02)
-        blocks = torch.empty(lib.mq_quantized_bytes(q, n, k), dtype=torch.uint8, device=dev)
-        rc = lib.mq_quantize_device(local_rank, q, w32.data_ptr(), n, k, blocks.data_ptr(), blocks.numel(), sh)
+        gen.manual_seed(1000 + i)
+        w32 = torch.randn((n * world, k), generator=gen, device=dev, dtype=torch.float32).mul_(0.02)
+        blocks = torch.empty(lib.mq_quantized_bytes(q, n * world, k), dtype=torch.uint8, device=dev)
+        rc = lib.mq_quantize_device(local_rank, q, w32.data_ptr(), n * world, k, blocks.data_ptr(), blocks.numel(), sh)
         if rc:
             raise RuntimeError(mq._lib.last_error())
         del w32
-        handles.append(mq.CudaWeight.from_device_blocks(blocks, q, n, k, device=local_rank, stream=stream))
+        handles.append(mq.CudaWeight.from_device_blocks(blocks, q, n * world, k, device=local_rank, stream=stream,
+                                                        row_range=(rank * n, (rank + 1) * n)))
         if keep_host:
             host_blocks.append(blocks.cpu().numpy())
         del blocks
-    gen.manual_seed(424242 + rank)
+    comm = mq.CudaComm.from_process_group(local_rank) if world > 1 else None
+    gen.manual_seed(424242)
     xs = {(m, k): torch.randn((m, k), generator=gen, device=dev, dtype=torch.float32)
           for (_, m, _, _, k) in prods}
-    ys = {(m, n): torch.empty((m, n), dtype=torch.float32, device=dev) for (_, m, _, n, _) in prods}
-    calls = [(handles[i].handle, xs[(m, k)].data_ptr(), m, k, ys[(m, n)].data_ptr(), n)
+    ys = {(m, n): torch.empty((m, n * world), dtype=torch.float32, device=dev) for (_, m, _, n, _) in prods}
+    calls = [(handles[i].handle, xs[(m, k)].data_ptr(), m, k, ys[(m, n)].data_ptr(), n * world)
              for i, (q, m, name, n, k) in enumerate(prods)]
-    bytes_per_step = sum(algo_bytes(q, n, k, m) for (q, m, _, n, k) in prods)
-    linear = lib.mq_linear
+    # whole-job algorithmic bytes: every rank's shard product (its weights, x, its output slice)
+    bytes_per_step = sum(world * algo_bytes(q, n, k, m) for (q, m, _, n, k) in prods)
+    if world > 1:
+        gather = lib.mq_linear_sharded_allgather
+
+        def linear(h, x, m, k, b, y, n, s):
+            return gather(h, x, m, k, b, y, n, comm.handle, s)
+    else:
+        linear = lib.mq_linear
 
     def step(stream_handle, events=None, s=0):
         for j, (h, x, m, k, y, n) in enumerate(calls):
@@ -256,7 +271,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     dominant = max(class_ms, key=class_ms.get)
     j = cls_first[dominant]
     q, m, _, n, k = prods[j]
-    dom_launches = cls_count[dominant] * _launches_for(lib, calls[j], sh, torch)
+    dom_launches = cls_count[dominant] * _launches_for(lib, linear, calls[j], sh, torch)
     dom_bytes_per_launch = cls_bytes[dominant] / dom_launches
     dom_ms_per_launch = class_ms[dominant] / dom_launches
     peak, peak_kind = peaks()
@@ -270,12 +285,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     hx = {key: t.cpu().pin_memory() for key, t in xs.items()}
     hy = {key: torch.empty(t.shape, dtype=torch.float32).pin_memory() for key, t in ys.items()}
     h2d = sum(4 * m * k for (_, m, _, _, k) in prods)
-    d2h = sum(4 * m * n for (_, m, _, n, _) in prods)
+    d2h = sum(4 * m * n * world for (_, m, _, n, _) in prods)
+
+    apis = [mq.ShardedLinear.from_shard(h, comm) if world > 1 else h for h in handles]
 
     def e2e_step():
         for i, (q, m, name, n, k) in enumerate(prods):
             xs[(m, k)].copy_(hx[(m, k)], non_blocking=True)
-            handles[i].linear(xs[(m, k)], out=ys[(m, n)], stream=stream)
+            apis[i].linear(xs[(m, k)], out=ys[(m, n)], stream=stream)
             hy[(m, n)].copy_(ys[(m, n)], non_blocking=True)
 
     if not args.no_e2e:
@@ -307,10 +324,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 (GGUF Q4_0/Q4_1 weights)",
             "data": "synthetic (seeded N(0,0.02) weights packed bit-exactly, N(0,1) activations)",
             "config": {"workload": args.workload,
-                       "products": "gate/up 14336x4096, down 4096x14336; Q4_0, Q4_1; M = 1, 4, 16",
+                       "products": "gate/up 14336x4096, down 4096x14336; Q4_0, Q4_1; M = 1, 4, 16"
+                                   + (f"; rows x{world}, row-sharded" if world > 1 else ""),
                        "bytes_per_step": bytes_per_step,
-                       "l2": "inputs larger than L2: 627 MB of distinct weights per step",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+                       "l2": "inputs larger than L2: 627 MB of distinct weights per GPU per step",
+                       "parallelism": f"tp{world}: row shards + NCCL all-gather per product" if world > 1
+                       else "single GPU"},
             "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": traffic, "algorithmic_bytes_per_launch": int(dom_bytes_per_launch),
@@ -325,8 +344,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         if cpu is not None:
             out["cpu_baseline"] = cpu
         print(json.dumps(out), flush=True)
+    del graph  # a graph holding NCCL calls is released before the communicators
+    torch.cuda.synchronize(dev)
     for h in handles:
         h.close()
+    if comm is not None:
+        comm.close()
     if world > 1:
         dist.destroy_process_group()
 
@@ -358,11 +381,11 @@ def elapsed_ms(a, b) -> float:
     return ms
 
 
-def _launches_for(lib, call, sh, torch) -> int:
+def _launches_for(lib, linear, call, sh, torch) -> int:
     """Kernel launches one product issues (read from the library's counter)."""
     h, x, m, k, y, n = call
     a = lib.mq_kernel_launches()
-    rc = lib.mq_linear(h, x, m, k, None, y, n, sh)
+    rc = linear(h, x, m, k, None, y, n, sh)
     torch.cuda.synchronize()
     if rc:
         raise RuntimeError("mq_linear failed")

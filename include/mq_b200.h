@@ -143,6 +143,35 @@ int mq_linear_ragged(const mq_weight *w, const float *x, const int *offsets, int
 int mq_linear_noalloc(const mq_weight *w, const float *x, int m, int ldx, const float *bias, float *y, int ldy,
                       void *stream);
 
+/* ---- Row-sharded linear across GPUs (one process or host thread per GPU).
+ * A weight of N = G*R rows is split into G equal output-row shards
+ * (mq_weight_shard_create with rows [r*R, (r+1)*R) on rank r). Each rank
+ * computes its R outputs and an NCCL all-gather over NVLink assembles the
+ * full [m, N] output on every rank; the result is bit-identical to mq_linear
+ * on the whole weight. No counterpart in the reference, which runs every
+ * linear on one device (`--device N`, src/main.cc:249-250); new surface for
+ * the multi-GPU row of the hot path. NCCL is loaded at run time
+ * (libnccl.so.2). */
+typedef struct mq_comm mq_comm;
+#define MQ_COMM_ID_BYTES 128
+
+/* A fresh communicator id (rank 0 creates it and shares it with the other
+ * ranks through the caller's own host channel). len >= MQ_COMM_ID_BYTES. */
+int mq_comm_unique_id(void *id, size_t len);
+
+/* Join the communicator of `nranks` ranks as `rank`, on `device`. Collective:
+ * every rank must call it with the same id. */
+int mq_comm_create(int device, int nranks, int rank, const void *id, size_t len, mq_comm **out);
+void mq_comm_destroy(mq_comm *c);
+
+/* y[i, n] for all n in [0, N) on every rank: this rank's shard product
+ * (+ bias[rank*R .. rank*R+R) when bias, the full [N] vector, is given) and
+ * an all-gather of the slices. x: device F32 [m, ldx] (full K); y: device F32
+ * [m, ldy] with ldy >= N. Stream-ordered on `stream`; every rank must call it
+ * with the same m, in the same order relative to its other collectives. */
+int mq_linear_sharded_allgather(const mq_weight *shard, const float *x, int m, int ldx, const float *bias,
+                                float *y, int ldy, mq_comm *comm, void *stream);
+
 /* Kernel selection for the next mq_linear calls on this thread:
  * 0 = automatic (default): the stream-K SIMT GEMV for m <= 4, the tcgen05
  *     decode GEMM for m <= 32, the tcgen05 prefill GEMM above;

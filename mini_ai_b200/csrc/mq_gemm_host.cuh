@@ -44,6 +44,31 @@ int workspace_for(int device, cudaStream_t s, size_t bytes, void **out) {
   return MQ_OK;
 }
 
+// Gather buffer of the row-sharded linear (mq_comm.cu), one per (device,
+// stream) and separate from the workspace the linear itself uses.
+std::map<std::pair<int, cudaStream_t>, Workspace> g_gather;
+
+}  // namespace
+
+int gather_workspace_for(int device, cudaStream_t s, size_t bytes, void **out) {
+  std::lock_guard<std::mutex> lock(g_ws_mu);
+  Workspace &w = g_gather[{device, s}];
+  if (w.bytes < bytes) {
+    if (w.ptr) {
+      MQ_CUDA(cudaStreamSynchronize(s));
+      MQ_CUDA(cudaFree(w.ptr));
+      w.ptr = nullptr;
+      w.bytes = 0;
+    }
+    MQ_CUDA(cudaMalloc(&w.ptr, bytes));
+    w.bytes = bytes;
+  }
+  *out = w.ptr;
+  return MQ_OK;
+}
+
+namespace {
+
 // Split-K fixup tickets, one zeroed array per (device, stream); each launch
 // leaves them at zero again.
 std::map<std::pair<int, cudaStream_t>, Workspace> g_tickets;
