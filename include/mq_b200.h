@@ -173,7 +173,7 @@ int mq_linear_sharded_allgather(const mq_weight *shard, const float *x, int m, i
                                 float *y, int ldy, mq_comm *comm, void *stream);
 
 /* Kernel selection for the next mq_linear calls on this thread:
- * 0 = automatic (default): the stream-K SIMT GEMV for m <= 4, the tcgen05
+ * 0 = automatic (default): the stream-K SIMT GEMV for m <= 2, the tcgen05
  *     decode GEMM for m <= 32, the tcgen05 prefill GEMM above;
  * 1 = force the stream-K SIMT GEMV, 2 = force the tcgen05 prefill GEMM,
  * 4 = force the tcgen05 decode GEMM (3 is not a mode; other values are

@@ -177,9 +177,9 @@ cudaError_t launch_tcdec_t(const CUtensorMap &tx, const DecArgs &a, int grid, cu
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  tcdec_kernel<QT, BN, NC><<<grid, kDecThreads, L::kAlloc, s>>>(tx, a);
+  const cudaError_t e = launch_pdl(tcdec_kernel<QT, BN, NC>, dim3(grid), dim3(kDecThreads), L::kAlloc, s, tx, a);
   count_launch();
-  return cudaGetLastError();
+  return e;
 }
 
 template <int QT>
@@ -213,6 +213,26 @@ int env_threshold(const char *name, int dflt) {
   return e && *e ? std::atoi(e) : dflt;
 }
 
+// Launch with programmatic stream serialization (the kernel may start while
+// the previous kernel of the stream finishes; it synchronises with
+// griddepcontrol.wait where it depends on it). MQ_PDL=0 launches normally.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args &&...args) {
+  static const bool on = env_threshold("MQ_PDL", 1) != 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = on ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // Largest activation count served by the decode kernels in automatic mode;
 // above it the tcgen05 prefill GEMM takes over.
 int decode_max_m() {
@@ -244,10 +264,9 @@ DecPlan tcdec_plan(const WeightView &w, int device, int max_grid) {
 int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const float *bias, float *y, int64_t ldy,
                  cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort) {
   const int bn = dec_tile_rows(mm);
-  dec_prep_kernel<<<bn, 1024, 0, s>>>(x, ldx, mm, w.cols, plan.kpad, bn, buf.x2, buf.xsum, buf.xinv,
-                                      w.qtype == MQ_Q4_1);
+  MQ_CUDA(launch_pdl(dec_prep_kernel, dim3(plan.steps, (bn + 7) / 8), dim3(256), 0, s, x, ldx, mm, w.cols, plan.kpad,
+                     bn, buf.x2, buf.xsum, buf.xinv, (int)(w.qtype == MQ_Q4_1)));
   count_launch();
-  MQ_CUDA(cudaGetLastError());
   CUtensorMap tx;
   int rc;
   if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf.x2, 2 * bn, plan.kpad, plan.kpad, 64, 2 * bn)))
@@ -283,15 +302,16 @@ int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
     const int bn = dec_tile_rows(mm);
     const size_t xbytes = (size_t)2 * bn * plan.kpad * 2;
     const size_t sbytes = (size_t)(plan.kpad / 32) * bn * 4;
+    const size_t ibytes = ((size_t)plan.steps * bn * 4 + 255) & ~size_t(255);
     const size_t pbytes = (size_t)plan.grid * 2 * kDecRows * bn * 4;
     void *ws = nullptr;
-    if ((rc = workspace_for(wt->device, s, xbytes + sbytes + 256 + pbytes + 1024, &ws))) return rc;
+    if ((rc = workspace_for(wt->device, s, xbytes + sbytes + ibytes + pbytes + 1024, &ws))) return rc;
     uint8_t *base = static_cast<uint8_t *>(ws);
     DecBuffers buf;
     buf.x2 = reinterpret_cast<__half *>(base);
     buf.xsum = reinterpret_cast<float *>(base + xbytes);
     buf.xinv = reinterpret_cast<float *>(base + xbytes + sbytes);
-    buf.partial = reinterpret_cast<float *>(base + ((xbytes + sbytes + 256 + 1023) & ~size_t(1023)));
+    buf.partial = reinterpret_cast<float *>(base + ((xbytes + sbytes + ibytes + 1023) & ~size_t(1023)));
     buf.tickets = tickets;
     buf.err = err_dev;
     if ((rc = tcdec_launch(w, x + (int64_t)i0 * ldx, mm, ldx, bias, y + (int64_t)i0 * ldy, ldy, s, plan, buf, 0)))
@@ -311,9 +331,9 @@ cudaError_t launch_sdec_t(const CUtensorMap &tx, const SdecArgs &a, int grid, cu
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  sdec_kernel<QT, MC><<<grid, kSdThreads, L::kAlloc, s>>>(tx, a);
+  const cudaError_t e = launch_pdl(sdec_kernel<QT, MC>, dim3(grid), dim3(kSdThreads), L::kAlloc, s, tx, a);
   count_launch();
-  return cudaGetLastError();
+  return e;
 }
 
 template <int QT>
@@ -327,7 +347,7 @@ cudaError_t launch_sdec_q(const CUtensorMap &tx, const SdecArgs &a, int grid, in
 
 // Largest activation count served by the stream-K SIMT GEMV (mq_sdec.cuh).
 int sdec_max_m() {
-  static const int v = env_threshold("MQ_SDEC_MAX_M", 4);
+  static const int v = env_threshold("MQ_SDEC_MAX_M", 2);
   return v;
 }
 
@@ -344,12 +364,16 @@ int run_sdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const floa
     return fail(MQ_ERR_TIMEOUT, "an earlier stream-K launch on device %d ran out of a bounded wait", wt->device);
   }
   const WeightView &w = wt->v;
-  const DecPlan plan = tcdec_plan(w, wt->device);
+  DecPlan plan = tcdec_plan(w, wt->device);
   int *tickets = nullptr;
   if ((rc = tickets_for(wt->device, s, (size_t)plan.tiles, &tickets))) return rc;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, wt->device);
   for (int i0 = 0; i0 < m; i0 += 4) {
     const int mm = std::min(4, m - i0);
     const int mc = mm == 1 ? 1 : (mm == 2 ? 2 : 4);
+    const int ctas_per_sm = 1;  // SdCfg<QT, mc>::kCtasPerSm
+    plan.grid = std::max(1, std::min(ctas_per_sm * sms, plan.tiles * plan.steps));
     const float *xs = x + (int64_t)i0 * ldx;
     int64_t ldxs = ldx;
     const bool copy = (reinterpret_cast<uintptr_t>(xs) & 15) != 0 || (ldx & 3) != 0;

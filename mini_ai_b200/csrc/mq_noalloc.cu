@@ -25,7 +25,7 @@ constexpr int kNaMaxDevices = 64;
 
 constexpr size_t kNaX = (size_t)2 * kNaMaxM * kNaMaxKpad * sizeof(__half);    // 1 MiB: hi rows, lo rows
 constexpr size_t kNaSum = (size_t)(kNaMaxKpad / 32) * kNaMaxM * sizeof(float);  // 32 KiB
-constexpr size_t kNaInv = 256;
+constexpr size_t kNaInv = (size_t)(kNaMaxKpad / 256) * kNaMaxM * sizeof(float);  // 4 KiB: per (step, row)
 constexpr size_t kNaPart = (size_t)kNaMaxGrid * 2 * 128 * kNaMaxM * sizeof(float);  // 2.5 MiB
 constexpr size_t kNaTickets = (size_t)kNaMaxTiles * sizeof(int);
 constexpr size_t kNaErr = 256;

@@ -10,7 +10,10 @@
 // in flight. A stage holds the step's weight chunk (packed quant rows, 128-byte
 // swizzle pre-applied, fp16 scales, Q4_1 mins: one linear bulk copy of
 // consecutive memory) and the fp32 activations of the step's 256 K, loaded by
-// TMA straight from x (no split kernel, no extra launch).
+// TMA straight from x (no split kernel, no extra launch). Launched with
+// programmatic stream serialization: the weight stream starts while the
+// previous kernel finishes; activations, outputs and workspace are touched
+// only after griddepcontrol.wait.
 //
 // Compute: thread = weight row of the tile. The 16 compute warps are 4 row
 // quarters x 4 block pairs: warp w owns rows 32(w%4).. and blocks
@@ -74,11 +77,15 @@ struct SdecArgs {
 
 template <int QT, int MC>
 struct SdCfg {
+  // Two CTAs per SM (more warps, half the ring each) measured slower than
+  // one CTA with the deeper ring: one per SM.
+  static constexpr int kCtasPerSm = 1;
   static constexpr int kPkBytes = step_pk_bytes(QT);
   static constexpr int kScBytes = step_sc_bytes(QT);
   static constexpr int kXBytes = MC * 256 * 4;
   static constexpr int kStage = kPkBytes + kScBytes + kXBytes;
-  static constexpr int ST = (200 * 1024 / kStage) < 8 ? (200 * 1024 / kStage) : 8;  // ring depth
+  static constexpr int kBudget = (kCtasPerSm == 2 ? 104 : 200) * 1024;
+  static constexpr int ST = (kBudget / kStage) < 8 ? (kBudget / kStage) : 8;  // ring depth
   static constexpr int kRedOff = ST * kStage;                                       // [4][128][MC] floats
   static constexpr int kBarOff = kRedOff + 4 * kSdRows * MC * 4;
   static constexpr int kBytes = kBarOff + 16 * ST + 16;
@@ -88,7 +95,7 @@ struct SdCfg {
 };
 
 template <int QT, int MC>
-__global__ void __launch_bounds__(kSdThreads, 1)
+__global__ void __launch_bounds__(kSdThreads, SdCfg<QT, MC>::kCtasPerSm)
     sdec_kernel(const __grid_constant__ CUtensorMap tm_x, const SdecArgs a) {
   using L = SdCfg<QT, MC>;
   constexpr int ST = L::ST;
@@ -111,11 +118,24 @@ __global__ void __launch_bounds__(kSdThreads, 1)
   }
   __syncthreads();
 
+  if (threadIdx.x == 0) sm100::griddep_launch_dependents();
   if (warp == kSdComputeWarps) {  // ------------------------- producer: one stage per step
     if (lane == 0) {
       sm100::prefetch_tmap(&tm_x);
-      int issued = 0;
-      for (int ls = 0; ls < nsteps; ++ls) {
+      // The weights are read-only: the first ring's worth streams in while
+      // the previous kernel of the stream (which may produce x) finishes.
+      const int pre = nsteps < ST ? nsteps : ST;
+      for (int ls = 0; ls < pre; ++ls) {
+        const int g = g0 + ls;
+        sm100::mbar_arrive_expect_tx(&full[ls], L::kStage);
+        sm100::bulk_load(smem + ls * L::kStage, chunk_ptr(a.w, g / S, g % S), L::kPkBytes + L::kScBytes, &full[ls]);
+      }
+      sm100::griddep_wait();
+      for (int ls = 0; ls < pre; ++ls)
+        sm100::tma_load_2d(smem + ls * L::kStage + L::kPkBytes + L::kScBytes, &tm_x, ((g0 + ls) % S) * 256, 0,
+                           &full[ls]);
+      int issued = pre;
+      for (int ls = pre; ls < nsteps; ++ls) {
         const int i = ls % ST;
         if (!sm100::mbar_wait_sleep(&empty[i], ((uint32_t)(ls / ST) & 1u) ^ 1u, a.err, abort, kSdWaitNs)) break;
         const int g = g0 + ls, k = g % S;
@@ -130,6 +150,7 @@ __global__ void __launch_bounds__(kSdThreads, 1)
         sm100::mbar_wait(&full[p % ST], (uint32_t)(p / ST) & 1u, nullptr, nullptr, kSdDrainNs);
     }
   } else {  // ------------------------------------------------ compute: thread = row, warp = (quarter, block pair)
+    sm100::griddep_wait();  // y, partial slots and tickets may still be in use by the previous kernel
     const int rq = warp & 3, bp = warp >> 2;
     const int r = 32 * rq + lane, sw = r & 7;
     const int qd = bp >> 1, j0 = 2 * (bp & 1);  // quad of the step, first block of the pair inside it

@@ -116,6 +116,16 @@ __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 
+// Programmatic dependent launch. launch_dependents lets the next kernel of
+// the stream (launched with programmatic stream serialization) start its
+// prologue now; wait blocks the calling thread until the previous kernel has
+// completed and its memory is visible. Both are no-ops without the launch
+// attribute.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Generic-proxy smem writes -> visible to the async proxy (tcgen05.mma reads).
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 

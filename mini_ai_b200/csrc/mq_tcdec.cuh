@@ -7,9 +7,9 @@
 //
 // Exactness scheme. The A operand holds the exact integers q - zp (fp16), not
 // the scaled weights, so no rounding or range issue is introduced by the
-// per-block fp16 scale; the activation rows are scaled by a power of two and
-// split into fp16 hi + lo (22 significant bits), stacked as the two halves of
-// the MMA's N dimension. Each 32-weight block accumulates into its own TMEM
+// per-block fp16 scale; each activation row is scaled, per 256-K step, by a
+// power of two and split into fp16 hi + lo (22 significant bits), stacked as
+// the two halves of the MMA's N dimension. Each 32-weight block accumulates into its own TMEM
 // slot, and drainer warps apply the block scale in fp32:
 //   acc += d_b * (D_b,hi + D_b,lo) (+ m_b * sum_b x).
 // Products of small integers and fp16 values are exact in the fp32
@@ -57,6 +57,9 @@
 //   warps 12..15   drainers: per group, TMEM -> registers, scale in fp32;
 //                  flush per tile (x row scale 2^-e, bias, store or partial +
 //                  ticket).
+// Launched with programmatic stream serialization after the activation split:
+// TMEM allocation and the weight stream start while the split still runs; the
+// activation TMA and the drainers wait for it (griddepcontrol.wait).
 // Every wait is bounded in time; a timeout raises the CTA abort flag and the
 // host-visible error flag, and all roles leave their loops (the drainers keep
 // their loop shape so that their named barriers still match). Before the TMEM
@@ -84,7 +87,7 @@ constexpr uint64_t kDecDrainNs = 20000000ull;
 struct DecArgs {
   WeightView w;
   int m;                 // activation rows (<= NC)
-  const float *xinv;     // [BN] 2^-e per activation row
+  const float *xinv;     // [steps][BN] 2^-e per (step, activation row)
   const float *xsum;     // [kpad / 32][BN] scaled block sums of x (Q4_1)
   const float *bias;
   float *y;
@@ -257,6 +260,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) sm100::griddep_launch_dependents();
 
   // Commit group of the last block of quad q: its completion frees the quad's
   // A slot and activation stage.
@@ -288,6 +292,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   } else if (warp == 2) {
     if (lane == 0) {  // ------------------------------------- TMA: activation tiles, one per quad
       sm100::prefetch_tmap(&tm_x);
+      sm100::griddep_wait();  // the activation split is the previous kernel
       int issued = 0;
       for (int q = 0; q < nquads; ++q) {
         const int i = q % XS;
@@ -430,6 +435,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       if (lane == 0) sm100::mbar_arrive(&pk_empty[pi]);
     }
   } else {  // ------------------------------------------------ drainers (TMEM lane = tile row)
+    sm100::griddep_wait();  // block sums, row scales, outputs and workspace
     const int qq = warp & 3;
     const int r = 32 * qq + lane;
     const uint32_t lane_base = (uint32_t)(32 * qq) << 16;
@@ -453,7 +459,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
           const float bias = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
           for (int c = 0; c < NC; ++c)
-            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = acc[c] * a.xinv[c] + bias;
+            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = acc[c] + bias;
         }
         return;
       }
@@ -485,7 +491,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
           const float bias = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
           for (int c = 0; c < NC; ++c)
-            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = tot[c] * a.xinv[c] + bias;
+            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = tot[c] + bias;
         }
         if (warp == 12 && lane == 0) a.tickets[tile] = 0;  // ready for the next launch
       }
@@ -510,6 +516,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       if constexpr (QT == MQ_Q4_1) mq = *reinterpret_cast<const uint4 *>(sc + kDecRows * 16 + r * 16);
       const uint32_t dw[4] = {dq.x, dq.y, dq.z, dq.w};
       const uint32_t mw[4] = {mq.x, mq.y, mq.z, mq.w};
+      float st[NC];  // this step's sum, in the step's activation scale
+#pragma unroll
+      for (int c = 0; c < NC; ++c) st[c] = 0.0f;
 #pragma unroll
       for (int gl = 0; gl < kGroupsPerStep; ++gl) {
         const int gi = ls * kGroupsPerStep + gl;
@@ -517,6 +526,48 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         ok = __all_sync(0xffffffffu, ok && sc_ok);
         sm100::tc_fence_after();
         const uint32_t dbase = tmem + lane_base + (uint32_t)(L::kDOff + (gi % ND) * L::kDCols);
+        if constexpr (N == 64) {
+          // 32 activation rows (G = 1): the hi and lo halves one after the other,
+          // so that a half, the step sum and the accumulator fit the registers.
+          const int jb = gl;
+          const __half2 d2 = *reinterpret_cast<const __half2 *>(&dw[jb >> 1]);
+          const float d = (jb & 1) ? __high2float(d2) : __low2float(d2);
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t vh[32];
+            if (ok) {
+              sm100::tmem_ld_32x32b_x32(dbase + (uint32_t)(32 * half), vh);
+              sm100::tmem_ld_wait();
+            } else {
+#pragma unroll
+              for (int c = 0; c < 32; ++c) vh[c] = 0u;
+            }
+#pragma unroll
+            for (int c = 0; c < NC; c += 2) {
+              const float2 r2 = __ffma2_rn(make_float2(d, d), make_float2(__uint_as_float(vh[c]), __uint_as_float(vh[c + 1])),
+                                           make_float2(st[c], st[c + 1]));
+              st[c] = r2.x, st[c + 1] = r2.y;
+            }
+          }
+          sm100::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) sm100::mbar_arrive(&d_empty[gi % ND]);
+          if constexpr (QT == MQ_Q4_1) {
+            const __half2 m2 = *reinterpret_cast<const __half2 *>(&mw[jb >> 1]);
+            const float mm = (jb & 1) ? __high2float(m2) : __low2float(m2);
+            const float4 *xs =
+                reinterpret_cast<const float4 *>(a.xsum + (int64_t)(kstep * kDecBlocksPerStep + jb) * BN);
+#pragma unroll
+            for (int c = 0; c < NC; c += 4) {
+              const float4 s4 = __ldg(xs + c / 4);
+              st[c] = fmaf(mm, s4.x, st[c]);
+              st[c + 1] = fmaf(mm, s4.y, st[c + 1]);
+              st[c + 2] = fmaf(mm, s4.z, st[c + 2]);
+              st[c + 3] = fmaf(mm, s4.w, st[c + 3]);
+            }
+          }
+          continue;
+        }
         // The whole group in one batch of loads and one wait; the D slot is
         // released before the arithmetic.
         uint32_t v[G * N];
@@ -541,10 +592,10 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 #pragma unroll
           for (int c = 0; c < NC; c += 2) {
             float2 r2 = __ffma2_rn(make_float2(d, d), make_float2(__uint_as_float(vb[c]), __uint_as_float(vb[c + 1])),
-                                   make_float2(acc[c], acc[c + 1]));
+                                   make_float2(st[c], st[c + 1]));
             r2 = __ffma2_rn(make_float2(d, d),
                             make_float2(__uint_as_float(vb[BN + c]), __uint_as_float(vb[BN + c + 1])), r2);
-            acc[c] = r2.x, acc[c + 1] = r2.y;
+            st[c] = r2.x, st[c + 1] = r2.y;
           }
           if constexpr (QT == MQ_Q4_1) {
             const __half2 m2 = *reinterpret_cast<const __half2 *>(&mw[jb >> 1]);
@@ -554,12 +605,23 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 #pragma unroll
             for (int c = 0; c < NC; c += 4) {
               const float4 s4 = __ldg(xs + c / 4);
-              acc[c] = fmaf(mm, s4.x, acc[c]);
-              acc[c + 1] = fmaf(mm, s4.y, acc[c + 1]);
-              acc[c + 2] = fmaf(mm, s4.z, acc[c + 2]);
-              acc[c + 3] = fmaf(mm, s4.w, acc[c + 3]);
+              st[c] = fmaf(mm, s4.x, st[c]);
+              st[c + 1] = fmaf(mm, s4.y, st[c + 1]);
+              st[c + 2] = fmaf(mm, s4.z, st[c + 2]);
+              st[c + 3] = fmaf(mm, s4.w, st[c + 3]);
             }
           }
+        }
+      }
+      {  // back to x's own scale: 2^-e of this step
+        const float4 *inv = reinterpret_cast<const float4 *>(a.xinv + (int64_t)kstep * BN);
+#pragma unroll
+        for (int c = 0; c < NC; c += 4) {
+          const float4 v4 = __ldg(inv + c / 4);
+          acc[c] = fmaf(st[c], v4.x, acc[c]);
+          acc[c + 1] = fmaf(st[c + 1], v4.y, acc[c + 1]);
+          acc[c + 2] = fmaf(st[c + 2], v4.z, acc[c + 2]);
+          acc[c + 3] = fmaf(st[c + 3], v4.w, acc[c + 3]);
         }
       }
       __syncwarp();
@@ -576,59 +638,64 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   }
 }
 
-// Activation split for the decode GEMM: one CTA per activation row (rows >= m
-// become zeros). Row i is scaled by 2^e_i (largest magnitude in [2^13, 2^14)),
-// split into fp16 hi + lo and written K-major into x2 ([2 bn][kpad]: hi rows,
-// then lo rows) in the decode kernel's K order (column c = 4t + s of a
-// block holds the original pair 8s + 2t, 8s + 2t + 1); block sums (Q4_1, in
-// natural order) and 2^-e_i are written alongside.
+// Activation split for the decode GEMM: one warp per (256-K step, activation
+// row), so the whole split is a single parallel pass (rows >= m become
+// zeros). The step's slice of row i is scaled by 2^e (largest magnitude in
+// [2^13, 2^14)), split into fp16 hi + lo and written K-major into x2
+// ([2 bn][kpad]: hi rows, then lo rows) in the decode kernel's K order
+// (column c = 4t + s of a block holds the original pair 8s + 2t, 8s + 2t + 1);
+// the scaled block sums (Q4_1, natural order) and 2^-e ([steps][bn]) are
+// written alongside. Grid: (steps, ceil(bn / 8)), 256 threads.
 __global__ void dec_prep_kernel(const float *__restrict__ x, int64_t ldx, int m, int K, int kpad, int bn,
                                 __half *__restrict__ x2, float *__restrict__ xsum, float *__restrict__ xinv,
                                 int want_sums) {
-  const int row = blockIdx.x;
+  // x may come from the previous kernel, and the split buffers may still be
+  // read by the previous decode launch; the decode GEMM itself may start now.
+  sm100::griddep_wait();
+  if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) sm100::griddep_launch_dependents();
+  const int lane = threadIdx.x & 31, row = blockIdx.y * 8 + (threadIdx.x >> 5), step = blockIdx.x;
+  if (row >= bn) return;
   const bool live = row < m;
   const float *xr = x + (int64_t)(live ? row : 0) * ldx;
-  __shared__ float red[32];
-  __shared__ float s_scale;
+  const int k0 = step * 256;
+  float v[8];
   float mx = 0.0f;
-  if (live)
-    for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(xr[k]));
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float v = 0.0f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) v = fmaxf(v, red[i]);
-    int e = 0;
-    if (v > 0.0f && isfinite(v)) {
-      int E;
-      frexpf(v, &E);
-      e = min(100, max(-100, 14 - E));
-    }
-    s_scale = ldexpf(1.0f, e);
-    xinv[row] = ldexpf(1.0f, -e);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {  // block j of the step, element `lane`
+    const int k = k0 + 32 * j + lane;
+    v[j] = (live && k < K) ? xr[k] : 0.0f;
+    mx = fmaxf(mx, fabsf(v[j]));
   }
-  __syncthreads();
-  const float sc = s_scale;
-  __half2 *h2 = reinterpret_cast<__half2 *>(x2 + (int64_t)row * kpad);
-  __half2 *l2 = reinterpret_cast<__half2 *>(x2 + (int64_t)(bn + row) * kpad);
-  for (int p = threadIdx.x; p < kpad / 2; p += blockDim.x) {  // p: fp16 pair = TMEM column c of block p / 16
-    const int c = p & 15, k = (p >> 4) * 32 + 8 * (c & 3) + 2 * (c >> 2);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  int e = 0;
+  if (mx > 0.0f && isfinite(mx)) {
+    int E;
+    frexpf(mx, &E);
+    e = min(100, max(-100, 14 - E));
+  }
+  const float sc = ldexpf(1.0f, e);
+  if (lane == 0) xinv[(int64_t)step * bn + row] = ldexpf(1.0f, -e);
+  if (want_sums) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float s = v[j] * sc;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) xsum[(int64_t)(step * 8 + j) * bn + row] = s;
+    }
+  }
+  __half2 *h2 = reinterpret_cast<__half2 *>(x2 + (int64_t)row * kpad + k0);
+  __half2 *l2 = reinterpret_cast<__half2 *>(x2 + (int64_t)(bn + row) * kpad + k0);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {  // fp16 pair p = TMEM column c of block p / 16
+    const int p = lane + 32 * j, c = p & 15;
+    const int k = k0 + (p >> 4) * 32 + 8 * (c & 3) + 2 * (c >> 2);
     const float v0 = (live && k < K) ? xr[k] * sc : 0.0f, v1 = (live && k + 1 < K) ? xr[k + 1] * sc : 0.0f;
     const __half2 hh = __floats2half2_rn(v0, v1);
     const float2 hf = __half22float2(hh);
     h2[p] = hh;
     l2[p] = __floats2half2_rn(v0 - hf.x, v1 - hf.y);
-  }
-  if (want_sums) {
-    const int nb = kpad >> 5;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int b = warp; b < nb; b += blockDim.x >> 5) {
-      const int k = 32 * b + lane;
-      float s = (live && k < K) ? xr[k] * sc : 0.0f;
-      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) xsum[(int64_t)b * bn + row] = s;
-    }
   }
 }
 
