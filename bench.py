@@ -278,7 +278,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     achieved = dom_bytes_per_launch / (dom_ms_per_launch * 1e-3) / 1e9
     traffic = _traffic(dominant)
 
-    value = world * bytes_per_step / (ms_per_step * 1e-3) / 1e9
+    value = bytes_per_step / (ms_per_step * 1e-3) / 1e9  # bytes_per_step is already the whole job's
 
     # End to end through the public API with host buffers (pinned), same stream.
     e2e_value, e2e_ms = None, None
@@ -310,7 +310,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_ms = float(t.item())
-        e2e_value = world * bytes_per_step / (e2e_ms / args.steps * 1e-3) / 1e9
+        e2e_value = bytes_per_step / (e2e_ms / args.steps * 1e-3) / 1e9
 
     cpu = None
     if keep_host:
