@@ -173,11 +173,11 @@ int mq_linear_sharded_allgather(const mq_weight *shard, const float *x, int m, i
                                 float *y, int ldy, mq_comm *comm, void *stream);
 
 /* Kernel selection for the next mq_linear calls on this thread:
- * 0 = automatic (default): the stream-K SIMT GEMV for m <= 2, the tcgen05
- *     decode GEMM for m <= 32, the tcgen05 prefill GEMM above;
+ * 0 = automatic (default): the tcgen05 int8 decode GEMV for m <= 4, the
+ *     tcgen05 fp16 decode GEMM for m <= 32, the tcgen05 prefill GEMM above;
  * 1 = force the stream-K SIMT GEMV, 2 = force the tcgen05 prefill GEMM,
- * 4 = force the tcgen05 decode GEMM (3 is not a mode; other values are
- * ignored). Returns the previous mode. */
+ * 3 = force the tcgen05 int8 decode GEMV, 4 = force the tcgen05 fp16 decode
+ * GEMM (other values are ignored). Returns the previous mode. */
 int mq_set_path(int mode);
 
 /* Number of kernels this library has launched in this process (all devices,

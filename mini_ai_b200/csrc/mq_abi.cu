@@ -293,7 +293,7 @@ int mq_weight_export(const mq_weight *w, void *dst, size_t dst_bytes) {
 
 int mq_set_path(int mode) {
   const int prev = g_path_mode;
-  if (mode == 0 || mode == 1 || mode == 2 || mode == 4) g_path_mode = mode;
+  if (mode >= 0 && mode <= 4) g_path_mode = mode;
   return prev;
 }
 
@@ -313,9 +313,10 @@ int mq_linear(const mq_weight *w, const float *x, int m, int ldx, const float *b
   if (!gemm_supported(w->device))
     return fail(MQ_ERR_UNSUPPORTED, "the kernels need an sm_100 device (device %d)", w->device);
   if (mode == 1) return run_sdec(w, x, m, ldx, bias, y, ldy, s);
+  if (mode == 3) return run_i8dec(w, x, m, ldx, bias, y, ldy, s);
   if (mode == 4) return run_tcdec(w, x, m, ldx, bias, y, ldy, s);
   if (mode == 2 || (mode == 0 && m > decode_max_m())) return run_gemm(w, x, m, ldx, bias, y, ldy, s);
-  if (m <= sdec_max_m()) return run_sdec(w, x, m, ldx, bias, y, ldy, s);
+  if (m <= i8dec_max_m()) return run_i8dec(w, x, m, ldx, bias, y, ldy, s);
   return run_tcdec(w, x, m, ldx, bias, y, ldy, s);
 }
 

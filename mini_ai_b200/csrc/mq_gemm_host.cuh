@@ -9,6 +9,7 @@
 #include <utility>
 
 #include "mq_gemm.cuh"
+#include "mq_i8dec.cuh"
 #include "mq_sdec.cuh"
 #include "mq_tcdec.cuh"
 
@@ -403,6 +404,91 @@ int run_sdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const floa
     default: e = launch_sdec_q<MQ_Q4_1>(tx, a, plan.grid, mc, s); break;
     }
     if (e != cudaSuccess) return cuda_fail(e, "stream-K GEMV launch");
+  }
+  return MQ_OK;
+}
+
+namespace {
+
+template <int QT, int MC>
+cudaError_t launch_i8dec_t(const CUtensorMap &tx, const I8Args &a, int grid, cudaStream_t s) {
+  using L = I8Cfg<QT, MC>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(i8dec_kernel<QT, MC>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const cudaError_t e = launch_pdl(i8dec_kernel<QT, MC>, dim3(grid), dim3(kI8Threads), L::kAlloc, s, tx, a);
+  count_launch();
+  return e;
+}
+
+template <int QT>
+cudaError_t launch_i8dec_q(const CUtensorMap &tx, const I8Args &a, int grid, int mc, cudaStream_t s) {
+  if (mc == 1) return launch_i8dec_t<QT, 1>(tx, a, grid, s);
+  if (mc == 2) return launch_i8dec_t<QT, 2>(tx, a, grid, s);
+  return launch_i8dec_t<QT, 4>(tx, a, grid, s);
+}
+
+}  // namespace
+
+// Largest activation count served by the int8 tensor-core decode kernel in
+// automatic mode (mq_i8dec.cuh); it takes up to 4 rows per launch.
+int i8dec_max_m() {
+  static const int v = env_threshold("MQ_I8DEC_MAX_M", 4);
+  return v;
+}
+
+// int8 tensor-core decode: up to 4 activation rows per launch.
+int run_i8dec(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
+              cudaStream_t s) {
+  int *err_dev = nullptr, *err_host = nullptr;
+  int rc = err_flag(wt->device, &err_dev, &err_host);
+  if (rc) return rc;
+  if (*(volatile int *)err_host) {
+    *(volatile int *)err_host = 0;
+    return fail(MQ_ERR_TIMEOUT, "an earlier int8 decode launch on device %d ran out of a bounded wait", wt->device);
+  }
+  const WeightView &w = wt->v;
+  const DecPlan plan = tcdec_plan(w, wt->device);
+  int *tickets = nullptr;
+  if ((rc = tickets_for(wt->device, s, (size_t)plan.tiles, &tickets))) return rc;
+  for (int i0 = 0; i0 < m; i0 += 4) {
+    const int mm = std::min(4, m - i0);
+    const int mc = mm == 1 ? 1 : (mm == 2 ? 2 : 4);
+    // The activation slices are read by TMA straight from x when its base and
+    // row stride are 16-byte aligned; otherwise x is first copied to an
+    // aligned scratch.
+    const float *xs = x + (int64_t)i0 * ldx;
+    int64_t ldxs = ldx;
+    const bool copy = (reinterpret_cast<uintptr_t>(xs) & 15) != 0 || (ldx & 3) != 0;
+    const int64_t ldc = ((int64_t)w.cols + 3) & ~int64_t(3);
+    const size_t pbytes = (size_t)plan.grid * 2 * kI8Rows * mc * 4;
+    const size_t cbytes = copy ? (size_t)mm * ldc * 4 : 0;
+    void *ws = nullptr;
+    if ((rc = workspace_for(wt->device, s, pbytes + cbytes + 1024, &ws))) return rc;
+    uint8_t *base = static_cast<uint8_t *>(ws);
+    if (copy) {
+      float *xc = reinterpret_cast<float *>(base + ((pbytes + 255) & ~size_t(255)));
+      MQ_CUDA(cudaMemcpy2DAsync(xc, (size_t)ldc * 4, xs, (size_t)ldx * 4, (size_t)w.cols * 4, (size_t)mm,
+                                cudaMemcpyDeviceToDevice, s));
+      xs = xc;
+      ldxs = ldc;
+    }
+    CUtensorMap tx;
+    if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xs, mm, w.cols, ldxs, 256, mc,
+                        CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return rc;
+    I8Args a{w, mm, bias, y + (int64_t)i0 * ldy, ldy, reinterpret_cast<float *>(base), tickets, plan.steps,
+             plan.tiles, err_dev, 0};
+    cudaError_t e;
+    switch (w.qtype) {
+    case MQ_Q8_0: e = launch_i8dec_q<MQ_Q8_0>(tx, a, plan.grid, mc, s); break;
+    case MQ_Q4_0: e = launch_i8dec_q<MQ_Q4_0>(tx, a, plan.grid, mc, s); break;
+    default: e = launch_i8dec_q<MQ_Q4_1>(tx, a, plan.grid, mc, s); break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "int8 decode launch");
   }
   return MQ_OK;
 }

@@ -1,0 +1,595 @@
+// tcgen05 int8 decode GEMV/GEMM for one to five activation rows.
+//
+// Decode streams every packed weight byte once, so the kernel must keep up
+// with HBM while doing as little SIMT work per weight as possible. Here the
+// tensor cores do all the multiplications on the weights' own integer codes:
+//
+//   y[i, n] = sum_b d[n,b] * sum_k q[n,b,k] * x[i, 32b + k]   (Q8_0: q signed)
+//           = sum_b d[n,b] * sum_k (q - 8) * x                (Q4_0: q unsigned)
+//           = sum_b (d[n,b] * sum_k q * x + m[n,b] * sum_k x) (Q4_1)
+//
+// Exactness scheme. Each activation row is scaled, per 256-K step, by a
+// power of two 2^e so that its largest magnitude lies in [2^21, 2^22), and
+// rounded to an integer X (22 significant bits: the rounding error is below
+// 2^-22 of the step's largest |x|). X is split into three signed 8-bit limbs,
+// X = l2 * 2^16 + l1 * 2^8 + l0, and the limbs are the rows of the MMA's B
+// operand (row 3t + l for activation row t, limb l). One tcgen05.mma of
+// kind::i8 (M = 128 weight rows, N = 16, K = 32 = one quant block) gives, per
+// weight row and block, the exact int32 sums L_l = sum_k q * l_l. The drainer
+// warps combine the limbs (in int32 for Q4_x, where |sum q X| < 2^31, so the
+// wrapping sum is exact; in fp32 for Q8_0) and apply the fp16 block scale in
+// fp32, and 2^-e once per step, so the result equals the reference's fp32 dot
+// up to accumulation-order rounding.
+//
+// Data flow per (128-row tile, 8-block step):
+//   weight chunk (packed codes, scales, mins): one bulk copy into the packed
+//   ring and one into the scale ring; a TMA load of the step's activation slice [256 K x
+//   rows] lands in the same scale stage, and prep warps turn it into the limb
+//   tile (B operand, 128-byte-swizzled K-major layout) and a header (2^-e and
+//   the integer block sums of X per activation row) in that stage;
+//   unpacker warps: packed bytes -> int8/uint8 codes in TMEM (tcgen05.st),
+//   one 64-column A slot per step (no conversion for Q8_0: the codes are
+//   moved as they are; Q4_x: two logic ops per 8 nibbles);
+//   four issuer threads: 2 MMAs each per step (A from TMEM, B from shared
+//   memory), each into its own 16-column D slot, one commit each per step;
+//   drainer warps: tcgen05.ld of the step's D slots, limb combine, block
+//   scales, accumulate; at the end of a tile: bias, store or stream-K partial.
+//
+// K order inside a block. The A columns of a block follow the device weight
+// layout: column 2t + h holds, in its four bytes p = 0..3,
+//   Q4_x: the codes of elements 2t + {0, 8, 1, 9}[p] + 16h,
+//   Q8_0: the codes of elements 2t + {0, 1, 8, 9}[p] + 16h,
+// and the B image's K slot 4c + p holds the limb of the same element.
+//
+// Persistent stream-K over the tile-major step space, as the other decode
+// kernels: a tile whose K loop is split across CTAs is completed by the last
+// contributor from at most two partial slots per CTA (deterministic order).
+// Warp roles (22 warps): warp 0 bulk copies of the packed codes; warp 21 bulk
+// copies of the scales and TMA loads of the activation slices; warps 1, 2, 3
+// and 20 MMA issue, one thread each, two of every step's 8 blocks each
+// (issuing a tcgen05.mma occupies its thread for about 80 ns, measured on
+// B200, so one issuer would add ~0.6 us to every step's latency); warp 1 also
+// allocates the TMEM; warps 4..7 prep (limb tiles), taking the steps in turn;
+// warps 8..15 unpackers (two per TMEM lane quarter, one quad of 4 blocks
+// each); warps 16..19 drainers (one per lane quarter). Every wait is
+// bounded in time; a timeout raises the CTA abort flag and the host-visible
+// error flag and every role leaves its loop (drainers keep their loop shape so
+// that their named barriers still match); in-flight bulk copies and MMAs are
+// waited for (bounded) before the TMEM is released.
+//
+// Reference semantics: QuantizedDotRow, src/quantized_tensor.cc:161-191, and
+// LinearKernel's fused bias, src/cuda_backend.cu:94-110.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include "mq_common.cuh"
+#include "mq_sm100.cuh"
+#include "mq_tcdec.cuh"
+
+namespace mq {
+
+constexpr int kI8Rows = 128;
+constexpr int kI8Warps = 22;
+constexpr int kI8Issuers = 4;       // MMA issue threads (warps 1, 2, 3, 20), 2 of a step's 8 blocks each
+constexpr int kI8Preps = 4;         // prep warps (4..7): step s is built by warp 4 + s % 4
+constexpr int kI8Threads = kI8Warps * 32;
+constexpr int kI8MaxM = 5;          // activation rows per launch: 3 limbs x 5 rows <= N = 16
+constexpr int kI8N = 16;            // MMA N (B rows)
+constexpr int kI8BTile = 4096;      // B tile of a step: 2 slabs x 16 rows x 128 B (128-byte swizzle)
+constexpr int kI8HdrInv = 0;        // header: 2^-e per activation row, float[8]
+constexpr int kI8HdrSx = 32;        // header: integer block sums of X, int32[8 blocks][8 rows]
+constexpr int kI8Done = 8;          // commit barriers (ring)
+constexpr uint64_t kI8WaitNs = 1000000000ull;
+constexpr uint64_t kI8DrainNs = 20000000ull;
+
+struct I8Args {
+  WeightView w;
+  int m;                 // activation rows (<= MC)
+  const float *bias;
+  float *y;
+  int64_t ldy;
+  float *partial;        // [gridDim.x][2][128][MC]: head / tail partial tile of every CTA
+  int *tickets;          // [tiles], zero between launches
+  int steps;             // packed steps per tile (the K loop)
+  int tiles;
+  int *err;
+  int nan_on_abort;
+};
+
+template <int QT, int MC>
+struct I8Cfg {
+  static constexpr int kPkBytes = step_pk_bytes(QT);            // packed codes of a step
+  static constexpr int kScBytes = step_sc_bytes(QT);            // scales (+ mins)
+  // scale stage: B tile | header | scales (+ mins) | activation slice [MC][256] f32
+  static constexpr int kSbHdr = kI8BTile;
+  static constexpr int kSbSc = kI8BTile + 512;
+  static constexpr int kSbX = kSbSc + kScBytes;
+  static constexpr int kXBytes = MC * 256 * 4;
+  static constexpr int kSbBytes = ((kSbX + kXBytes) + 1023) / 1024 * 1024;
+  static constexpr int SS = 8;                                  // scale / B stages
+  static constexpr int kPsFit = (220 * 1024 - SS * kSbBytes) / kPkBytes;
+  static constexpr int PS = kPsFit < 8 ? kPsFit : 8;            // packed stages
+  static constexpr int NA = 2;                                  // A slots in TMEM (64 columns each)
+  static constexpr int ND = 3;                                  // D slots in TMEM (128 columns each)
+  static constexpr int kACols = 64, kDCols = 8 * kI8N, kDOff = NA * kACols;
+  static_assert(kDOff + ND * kDCols <= 512, "TMEM budget");
+  static constexpr int kPkOff = 0;
+  static constexpr int kSbOff = kPkOff + PS * kPkBytes;
+  static constexpr int kBarOff = kSbOff + SS * kSbBytes;
+  static constexpr int kNumBars = 2 * PS + 3 * SS + NA + ND + kI8Done + kI8Issuers;
+  static_assert(SS % kI8Preps == 0, "a prep warp owns every phase of its stages");
+  static constexpr int kBytes = kBarOff + 8 * kNumBars + 16;
+  static constexpr int kAlloc = kBytes + 1024;
+  static_assert(PS >= 3 && kAlloc <= 227 * 1024, "shared memory budget");
+  // D columns the drainers read per block (3 limbs per activation row) and
+  // blocks per batch of TMEM loads (32 registers a batch).
+  static constexpr int NCOL = MC <= 1 ? 4 : (MC <= 2 ? 8 : 16);
+  static constexpr int BB = 32 / NCOL;
+  static_assert(3 * MC <= NCOL || NCOL == 16, "limb columns");
+  static_assert(MC <= kI8MaxM, "activation rows");
+};
+
+// Instruction descriptor, kind::i8: A unsigned (Q4_x) or signed (Q8_0) 8-bit,
+// B signed 8-bit, D int32, both K-major.
+__host__ __device__ constexpr uint32_t idesc_i8_s32(int M, int N, bool a_signed) {
+  return (2u << 4) | ((a_signed ? 1u : 0u) << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+
+// D[tmem] = A[tmem] x B[smem]^T, kind::i8 (no accumulation: each block has its own slot).
+__device__ __forceinline__ void umma_i8_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, 0, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_x4(uint32_t taddr, uint32_t *r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, uint32_t *r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+template <int NCOL>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t *r) {
+  if constexpr (NCOL == 4) {
+    tmem_ld_x4(taddr, r);
+  } else if constexpr (NCOL == 8) {
+    tmem_ld_x8(taddr, r);
+  } else {
+    tmem_ld_x16(taddr, *reinterpret_cast<uint32_t(*)[16]>(r));
+  }
+}
+
+// Element (0..31) of a quant block whose code sits in byte p of A column c
+// (see "K order inside a block").
+__host__ __device__ inline int i8_slot_elem(int qtype, int c, int p) {
+  const int t = c >> 1, h = c & 1;
+  const int q4[4] = {0, 8, 1, 9}, q8[4] = {0, 1, 8, 9};
+  return 2 * t + (qtype == MQ_Q8_0 ? q8[p] : q4[p]) + 16 * h;
+}
+
+template <int QT, int MC>
+__global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const __grid_constant__ CUtensorMap tm_x, const I8Args a) {
+  using L = I8Cfg<QT, MC>;
+  constexpr int PS = L::PS, SS = L::SS, NA = L::NA, ND = L::ND, NCOL = L::NCOL, BB = L::BB;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::kBarOff);
+  uint64_t *pk_full = bars, *pk_empty = pk_full + PS;
+  // sbx_full: scales + activation slice landed (TMA); sb_full: B tile and header built (prep warps)
+  uint64_t *sb_full = pk_empty + PS, *sb_empty = sb_full + SS, *sbx_full = sb_empty + SS;
+  // a_full: per A slot; d_empty: per D slot; done: commit ring (4 commits a step); fin: per issuer
+  uint64_t *a_full = sbx_full + SS, *d_empty = a_full + NA, *done = d_empty + ND, *fin = done + kI8Done;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::kNumBars);
+  volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  __shared__ int s_last;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = a.steps, T = a.tiles * a.steps, GR = gridDim.x, cta = blockIdx.x;
+  const int g0 = dec_first_step(cta, GR, T), g1 = dec_first_step(cta + 1, GR, T);
+  const int nsteps = g1 - g0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < PS; ++i) sm100::mbar_init(&pk_full[i], 1), sm100::mbar_init(&pk_empty[i], 8);
+    for (int i = 0; i < SS; ++i)
+      sm100::mbar_init(&sb_full[i], 1), sm100::mbar_init(&sb_empty[i], 4), sm100::mbar_init(&sbx_full[i], 1);
+    for (int i = 0; i < NA; ++i) sm100::mbar_init(&a_full[i], 8);
+    for (int i = 0; i < ND; ++i) sm100::mbar_init(&d_empty[i], 4);
+    for (int i = 0; i < kI8Done; ++i) sm100::mbar_init(&done[i], kI8Issuers);
+    for (int i = 0; i < kI8Issuers; ++i) sm100::mbar_init(&fin[i], 1);
+    *abort = 0;
+    sm100::fence_mbar_init();
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_slot, 512);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) sm100::griddep_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {  // --------------------------------------- bulk copies: packed codes
+      // (An L2 bulk prefetch ahead of this ring measured slower: it goes
+      // through the same per-SM TMA engine and delays the ring's own copies.)
+      int issued = 0;
+      for (int ls = 0; ls < nsteps; ++ls) {
+        const int g = g0 + ls, i = ls % PS;
+        if (ls >= PS &&
+            !sm100::mbar_wait_sleep(&pk_empty[i], ((uint32_t)(ls / PS) & 1u) ^ 1u, a.err, abort, kI8WaitNs))
+          break;
+        sm100::mbar_arrive_expect_tx(&pk_full[i], L::kPkBytes);
+        sm100::bulk_load(smem + L::kPkOff + i * L::kPkBytes, chunk_ptr(a.w, g / S, g % S), L::kPkBytes, &pk_full[i]);
+        issued = ls + 1;
+      }
+      // No copy may still be landing when the CTA exits.
+      for (int p = issued - PS < 0 ? 0 : issued - PS; p < issued; ++p)
+        sm100::mbar_wait(&pk_full[p % PS], (uint32_t)(p / PS) & 1u, nullptr, nullptr, kI8DrainNs);
+    }
+  } else if (warp == 21) {
+    if (lane == 0) {  // --------------------------------------- bulk copies: scales (+ mins), activation slices
+      sm100::prefetch_tmap(&tm_x);
+      auto issue_sc = [&](int ls) {
+        const int g = g0 + ls, i = ls % SS;
+        sm100::mbar_arrive_expect_tx(&sbx_full[i], L::kScBytes + L::kXBytes);
+        sm100::bulk_load(smem + L::kSbOff + i * L::kSbBytes + L::kSbSc, chunk_ptr(a.w, g / S, g % S) + L::kPkBytes,
+                         L::kScBytes, &sbx_full[i]);
+      };
+      auto issue_x = [&](int ls) {  // rows >= m and K past the end read as zeros
+        const int i = ls % SS;
+        sm100::tma_load_2d(smem + L::kSbOff + i * L::kSbBytes + L::kSbX, &tm_x, ((g0 + ls) % S) * 256, 0, &sbx_full[i]);
+      };
+      // The scales are read-only: the first ring's worth streams in while the
+      // previous kernel of the stream (which may produce x) still runs.
+      const int pre = nsteps < SS ? nsteps : SS;
+      for (int ls = 0; ls < pre; ++ls) issue_sc(ls);
+      sm100::griddep_wait();
+      for (int ls = 0; ls < pre; ++ls) issue_x(ls);
+      int issued = pre;
+      for (int ls = pre; ls < nsteps; ++ls) {
+        if (!sm100::mbar_wait_sleep(&sb_empty[ls % SS], ((uint32_t)(ls / SS) & 1u) ^ 1u, a.err, abort, kI8WaitNs))
+          break;
+        issue_sc(ls);
+        issue_x(ls);
+        issued = ls + 1;
+      }
+      for (int p = issued - SS < 0 ? 0 : issued - SS; p < issued; ++p)
+        sm100::mbar_wait(&sbx_full[p % SS], (uint32_t)(p / SS) & 1u, nullptr, nullptr, kI8DrainNs);
+    }
+  } else if (warp >= 4 && warp < 4 + kI8Preps) {  // ---------- prep: activation slice -> limb tile + header
+    // Lane l builds the 4-slot words w = l and l + 32 of each limb row (word
+    // w: block w / 8, A column w % 8). A row's slice is scaled by 2^e (largest
+    // magnitude in [2^21, 2^22)) and rounded to integers X (round to nearest
+    // even through the fp32 magic 1.5 * 2^23), split into balanced limbs
+    // X = l0 + 2^8 l1 + 2^16 l2; the header holds 2^-e and the integer block
+    // sums of X. A non-finite value in the slice makes 2^-e NaN, so that row's
+    // outputs become NaN. Rows >= m (zero filled by the TMA load) get zero limbs.
+    const int pw = warp - 4;
+    auto word_off = [](int n, int w) {  // byte offset of word w of B row n inside the B tile
+      const int j = w >> 3, c8 = w & 7;
+      const int pos = 32 * (j & 3) + 4 * c8;  // byte inside the slab's 128-byte row
+      return (j >> 2) * 2048 + (n >> 3) * 1024 + (n & 7) * 128 + (((pos >> 4) ^ (n & 7)) << 4) + (pos & 15);
+    };
+    for (int ls = pw; ls < nsteps; ls += kI8Preps) {
+      const int i = ls % SS;
+      if (!__all_sync(0xffffffffu,
+                      sm100::mbar_wait_sleep(&sbx_full[i], (uint32_t)(ls / SS) & 1u, a.err, abort, kI8WaitNs)))
+        break;
+      uint8_t *stage = smem + L::kSbOff + i * L::kSbBytes;
+      const float *xs = reinterpret_cast<const float *>(stage + L::kSbX);
+      float *inv = reinterpret_cast<float *>(stage + L::kSbHdr + kI8HdrInv);
+      int *sx = reinterpret_cast<int *>(stage + L::kSbHdr + kI8HdrSx);
+#pragma unroll
+      for (int t = 0; t < MC; ++t) {
+        // slots 4c + p of column c = 2 tt + h hold the elements 2 tt + {0, 8, 1, 9} + 16 h (Q4_x) or
+        // 2 tt + {0, 1, 8, 9} + 16 h (Q8_0): two float2 loads per word
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int w = lane + 32 * u, j = w >> 3, c8 = w & 7;
+          const float *bx = xs + t * 256 + 32 * j + 2 * (c8 >> 1) + 16 * (c8 & 1);
+          const float2 lo = *reinterpret_cast<const float2 *>(bx), hi = *reinterpret_cast<const float2 *>(bx + 8);
+          if constexpr (QT == MQ_Q8_0) {
+            v[4 * u + 0] = lo.x, v[4 * u + 1] = lo.y, v[4 * u + 2] = hi.x, v[4 * u + 3] = hi.y;
+          } else {
+            v[4 * u + 0] = lo.x, v[4 * u + 1] = hi.x, v[4 * u + 2] = lo.y, v[4 * u + 3] = hi.y;
+          }
+        }
+        uint32_t mb = 0u;  // largest |x| bits (integer order = magnitude order, NaN above Inf)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) mb = max(mb, __float_as_uint(v[q]) & 0x7fffffffu);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+        const bool finite = mb < 0x7f800000u;
+        // mx = f * 2^E with f in [0.5, 1): E = biased exponent - 126 (subnormal slices use E = -125)
+        const int be = (int)(mb >> 23);
+        const int e = (mb == 0u || !finite) ? 0 : min(126, max(-126, 22 - ((be > 0 ? be : 1) - 126)));
+        const float sc = __uint_as_float((uint32_t)(127 + e) << 23);
+        int X[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          X[q] = finite ? (int)(__float_as_uint(fmaf(v[q], sc, 12582912.0f)) - 0x4B400000u) : 0;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int w = lane + 32 * u;
+          uint32_t b0[4], b1[4], b2[4];
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const int xv = X[4 * u + p];
+            const int x1 = (xv - (int)(int8_t)xv) >> 8;  // balanced: l0 = sext(low byte)
+            const int l2 = (x1 - (int)(int8_t)x1) >> 8;
+            b0[p] = (uint32_t)xv & 255u, b1[p] = (uint32_t)x1 & 255u, b2[p] = (uint32_t)l2 & 255u;
+          }
+          const uint32_t w0 = b0[0] | (b0[1] << 8) | (b0[2] << 16) | (b0[3] << 24);
+          const uint32_t w1 = b1[0] | (b1[1] << 8) | (b1[2] << 16) | (b1[3] << 24);
+          const uint32_t w2 = b2[0] | (b2[1] << 8) | (b2[2] << 16) | (b2[3] << 24);
+          *reinterpret_cast<uint32_t *>(stage + word_off(3 * t + 0, w)) = w0;
+          *reinterpret_cast<uint32_t *>(stage + word_off(3 * t + 1, w)) = w1;
+          *reinterpret_cast<uint32_t *>(stage + word_off(3 * t + 2, w)) = w2;
+        }
+        // integer block sums: word w of lane l belongs to block w / 8 = lane / 8 (+ 4)
+        int s0 = X[0] + X[1] + X[2] + X[3], s1 = X[4] + X[5] + X[6] + X[7];
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) {
+          s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+          s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        }
+        if ((lane & 7) == 0) {
+          sx[(lane >> 3) * 8 + t] = s0;
+          sx[(4 + (lane >> 3)) * 8 + t] = s1;
+        }
+        if (lane == 0) inv[t] = finite ? __uint_as_float((uint32_t)(127 - e) << 23) : __int_as_float(0x7fc00000);
+      }
+      sm100::fence_proxy_async_smem();  // the MMAs read the tile through the async proxy
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&sb_full[i]);
+    }
+  } else if ((warp >= 1 && warp <= 3) || warp == 20) {
+    const int issuer = warp == 20 ? 3 : warp - 1;
+    if (lane == 0) {  // --------------------------------------- MMA issue: blocks 2 issuer, 2 issuer + 1 of every step
+      constexpr uint32_t idesc = idesc_i8_s32(kI8Rows, kI8N, QT == MQ_Q8_0);
+      for (int ls = 0; ls < nsteps; ++ls) {
+        bool ok = sm100::mbar_wait(&a_full[ls % NA], (uint32_t)(ls / NA) & 1u, a.err, abort, kI8WaitNs);
+        ok = ok && sm100::mbar_wait(&sb_full[ls % SS], (uint32_t)(ls / SS) & 1u, a.err, abort, kI8WaitNs);
+        ok = ok && sm100::mbar_wait(&d_empty[ls % ND], ((uint32_t)(ls / ND) & 1u) ^ 1u, a.err, abort, kI8WaitNs);
+        if (!ok) break;
+        sm100::tc_fence_after();
+        const uint32_t abase = tmem + (uint32_t)((ls % NA) * L::kACols);
+        const uint32_t dbase = tmem + (uint32_t)(L::kDOff + (ls % ND) * L::kDCols);
+        const uint64_t bdesc = sm100::umma_desc_sw128(sm100::smem_u32(smem + L::kSbOff + (ls % SS) * L::kSbBytes));
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          // block j: slab j / 4 (2 KB), K offset 32 * (j % 4) bytes inside the 128-byte row
+          const int j = 2 * issuer + jj;
+          const uint32_t off = (uint32_t)((j >> 2) * 2048 + (j & 3) * 32);
+          umma_i8_tmem_a(dbase + (uint32_t)(j * kI8N), abase + (uint32_t)(8 * j), bdesc + (off >> 4), idesc);
+        }
+        sm100::umma_commit(&done[ls % kI8Done]);
+      }
+      // Everything issued has completed before the TMEM is released.
+      sm100::umma_commit(&fin[issuer]);
+      sm100::mbar_wait(&fin[issuer], 0u, nullptr, nullptr, kI8DrainNs);
+    }
+  } else if (warp >= 8 && warp < 16) {  // ----------------------- unpackers: packed bytes -> codes in TMEM
+    const int qq = warp & 3;           // TMEM lane quarter
+    const int h = (warp - 8) >> 2;     // quad of the step: A columns 32h..32h+31 of a slot
+    const int r = 32 * qq + lane;      // tile row
+    const int sw = r & 7;
+    const uint32_t lane_base = (uint32_t)(32 * qq) << 16;
+    for (int ls = 0; ls < nsteps; ++ls) {
+      const int pi = ls % PS;
+      // tcgen05.st is warp-collective: every wait result is made warp-uniform.
+      bool ok = __all_sync(0xffffffffu,
+                           sm100::mbar_wait_sleep(&pk_full[pi], (uint32_t)(ls / PS) & 1u, a.err, abort, kI8WaitNs));
+      if (ok && ls >= NA) {  // the A slot is free once the MMAs of step ls - NA completed
+        const int pd = ls - NA;
+        ok = __all_sync(0xffffffffu, sm100::mbar_wait_sleep(&done[pd % kI8Done], (uint32_t)(pd / kI8Done) & 1u, a.err,
+                                                            abort, kI8WaitNs));
+      }
+      if (!ok) break;
+      // The quad's packed bytes go to registers first; the stage is released
+      // before they are converted and stored to TMEM.
+      uint32_t col[32];  // [block j of the quad][8 columns]
+      if constexpr (QT == MQ_Q8_0) {
+        const uint8_t *prow = smem + L::kPkOff + pi * L::kPkBytes + h * (kI8Rows * 128) + r * 128;
+        uint32_t cw[8][4];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 v = *reinterpret_cast<const uint4 *>(prow + ((c ^ sw) << 4));
+          cw[c][0] = v.x, cw[c][1] = v.y, cw[c][2] = v.z, cw[c][3] = v.w;
+        }
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&pk_empty[pi]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            col[8 * j + 2 * t] = cw[2 * t + (j >> 1)][2 * (j & 1)];
+            col[8 * j + 2 * t + 1] = cw[2 * t + (j >> 1)][2 * (j & 1) + 1];
+          }
+      } else {
+        const uint8_t *prow = smem + L::kPkOff + pi * L::kPkBytes + r * 128;
+        uint4 v4[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) v4[t] = *reinterpret_cast<const uint4 *>(prow + (((4 * h + t) ^ sw) << 4));
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&pk_empty[pi]);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const uint32_t wv[4] = {v4[t].x, v4[t].y, v4[t].z, v4[t].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            col[8 * j + 2 * t] = wv[j] & 0x0F0F0F0Fu;
+            col[8 * j + 2 * t + 1] = (wv[j] >> 4) & 0x0F0F0F0Fu;
+          }
+        }
+      }
+      tmem_st_x32(tmem + lane_base + (uint32_t)((ls % NA) * L::kACols + 32 * h), col);
+      tmem_st_wait();
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        sm100::mbar_arrive(&a_full[ls % NA]);
+      }
+    }
+  } else if (warp >= 16) {  // -------------------------------------- drainers (TMEM lane = tile row)
+    sm100::griddep_wait();  // outputs, partial slots and tickets may still be in use by the previous kernel
+    const int qq = warp & 3;
+    const int r = 32 * qq + lane;
+    const uint32_t lane_base = (uint32_t)(32 * qq) << 16;
+    float acc[MC];
+    int cur = -1;
+    // Completes the tile's output: directly when this CTA owns the whole K loop
+    // of the tile, else through the head/tail partial slots and the tile's
+    // ticket (the last contributor sums the slots in CTA order).
+    auto flush = [&](int tile) {
+      const bool aborted = *abort;
+      if (aborted && a.nan_on_abort) {
+#pragma unroll
+        for (int c = 0; c < MC; ++c) acc[c] = __int_as_float(0x7fc00000);
+      }
+      const bool write = !aborted || a.nan_on_abort;
+      const int n = tile * kI8Rows + r;
+      const bool row_ok = n < a.w.rows;
+      const int tg0 = tile * S, tg1 = tg0 + S;
+      if (tg0 >= g0 && tg1 <= g1) {
+        if (write && row_ok) {
+          const float bias = a.bias ? a.bias[n] : 0.0f;
+#pragma unroll
+          for (int c = 0; c < MC; ++c)
+            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = acc[c] + bias;
+        }
+        return;
+      }
+      const int kind = (tile == g0 / S) ? 0 : 1;
+      float *slot = a.partial + (((int64_t)cta * 2 + kind) * kI8Rows + r) * MC;
+#pragma unroll
+      for (int c = 0; c < MC; ++c) slot[c] = acc[c];
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const int cf = dec_cta_of_step(tg0, GR, T), cl = dec_cta_of_step(tg1 - 1, GR, T);
+      if (warp == 16 && lane == 0) s_last = atomicAdd(&a.tickets[tile], 1) == cl - cf;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (s_last) {
+        __threadfence();
+        float tot[MC];
+#pragma unroll
+        for (int c = 0; c < MC; ++c) tot[c] = 0.0f;
+        for (int cc = cf; cc <= cl; ++cc) {  // fixed CTA order: deterministic
+          const int kk = (tile == dec_first_step(cc, GR, T) / S) ? 0 : 1;
+          const float *ps = a.partial + (((int64_t)cc * 2 + kk) * kI8Rows + r) * MC;
+#pragma unroll
+          for (int c = 0; c < MC; ++c) tot[c] += __ldcg(ps + c);
+        }
+        if (write && row_ok) {
+          const float bias = a.bias ? a.bias[n] : 0.0f;
+#pragma unroll
+          for (int c = 0; c < MC; ++c)
+            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = tot[c] + bias;
+        }
+        if (warp == 16 && lane == 0) a.tickets[tile] = 0;  // ready for the next launch
+      }
+      // the next tile's slot may reuse this CTA's slot only after s_last is read
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+    };
+    for (int ls = 0; ls < nsteps; ++ls) {
+      const int g = g0 + ls, tile = g / S;
+      if (tile != cur) {
+        if (cur >= 0) flush(cur);
+        cur = tile;
+#pragma unroll
+        for (int c = 0; c < MC; ++c) acc[c] = 0.0f;
+      }
+      const int si = ls % SS;
+      // Failed waits do not leave the loop: every drainer must run the same
+      // sequence of flushes (they synchronise on a named barrier).
+      bool ok = sm100::mbar_wait_sleep(&sb_full[si], (uint32_t)(ls / SS) & 1u, a.err, abort, kI8WaitNs);
+      ok = ok && sm100::mbar_wait_sleep(&done[ls % kI8Done], (uint32_t)(ls / kI8Done) & 1u, a.err, abort, kI8WaitNs);
+      ok = __all_sync(0xffffffffu, ok);
+      sm100::tc_fence_after();
+      const uint8_t *sb = smem + L::kSbOff + si * L::kSbBytes;
+      const uint4 dq = *reinterpret_cast<const uint4 *>(sb + L::kSbSc + r * 16);
+      uint4 mq4 = make_uint4(0u, 0u, 0u, 0u);
+      if constexpr (QT == MQ_Q4_1) mq4 = *reinterpret_cast<const uint4 *>(sb + L::kSbSc + kI8Rows * 16 + r * 16);
+      const uint32_t dw[4] = {dq.x, dq.y, dq.z, dq.w};
+      const uint32_t mw[4] = {mq4.x, mq4.y, mq4.z, mq4.w};
+      const float *inv = reinterpret_cast<const float *>(sb + L::kSbHdr + kI8HdrInv);
+      const int *sx = reinterpret_cast<const int *>(sb + L::kSbHdr + kI8HdrSx);
+      const uint32_t dbase = tmem + lane_base + (uint32_t)(L::kDOff + (ls % ND) * L::kDCols);
+      float st[MC];  // this step's sum, in the step's activation scale
+#pragma unroll
+      for (int c = 0; c < MC; ++c) st[c] = 0.0f;
+#pragma unroll
+      for (int b0 = 0; b0 < 8; b0 += BB) {
+        uint32_t v[BB * NCOL];
+        if (ok) {
+#pragma unroll
+          for (int jb = 0; jb < BB; ++jb) tmem_ld_cols<NCOL>(dbase + (uint32_t)((b0 + jb) * kI8N), &v[jb * NCOL]);
+          sm100::tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int c = 0; c < BB * NCOL; ++c) v[c] = 0u;
+        }
+        if (b0 + BB == 8) {  // the D slot is released before the last batch's arithmetic
+          sm100::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) sm100::mbar_arrive(&d_empty[ls % ND]);
+        }
+#pragma unroll
+        for (int jb = 0; jb < BB; ++jb) {
+          const int j = b0 + jb;
+          const __half2 d2 = *reinterpret_cast<const __half2 *>(&dw[j >> 1]);
+          const float d = (j & 1) ? __high2float(d2) : __low2float(d2);
+          float mn = 0.0f;
+          if constexpr (QT == MQ_Q4_1) {
+            const __half2 m2 = *reinterpret_cast<const __half2 *>(&mw[j >> 1]);
+            mn = (j & 1) ? __high2float(m2) : __low2float(m2);
+          }
+          const uint32_t *vb = &v[jb * NCOL];
+#pragma unroll
+          for (int c = 0; c < MC; ++c) {
+            const int l0 = (int)vb[3 * c], l1 = (int)vb[3 * c + 1], l2 = (int)vb[3 * c + 2];
+            if constexpr (QT == MQ_Q8_0) {
+              const int v01 = l0 + (int)((uint32_t)l1 << 8);  // |.| < 2^27: exact
+              st[c] = fmaf(d, fmaf((float)l2, 65536.0f, (float)v01), st[c]);
+            } else {
+              // sum q * X fits int32, so the wrapping combination is exact.
+              int vv = (int)((uint32_t)l0 + ((uint32_t)l1 << 8) + ((uint32_t)l2 << 16));
+              if constexpr (QT == MQ_Q4_0) {
+                vv = (int)((uint32_t)vv - ((uint32_t)sx[j * 8 + c] << 3));
+                st[c] = fmaf(d, (float)vv, st[c]);
+              } else {
+                st[c] = fmaf(d, (float)vv, fmaf(mn, (float)sx[j * 8 + c], st[c]));
+              }
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < MC; ++c) acc[c] = fmaf(st[c], inv[c], acc[c]);
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&sb_empty[si]);
+    }
+    if (cur >= 0) flush(cur);
+  }
+
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace mq

@@ -209,7 +209,7 @@ def test_dimension_mismatch_raises(mq, cuda_device):
     assert "CUDA devices=" in mq.CudaDeviceInfo()
 
 
-PATHS = {1: "streamk_simt_gemv", 4: "tcgen05_decode", 2: "tcgen05_gemm"}
+PATHS = {1: "streamk_simt_gemv", 3: "tcgen05_i8_decode", 4: "tcgen05_decode", 2: "tcgen05_gemm"}
 
 
 @pytest.mark.parametrize("path", sorted(PATHS), ids=lambda p: PATHS[p])
@@ -217,7 +217,8 @@ PATHS = {1: "streamk_simt_gemv", 4: "tcgen05_decode", 2: "tcgen05_gemm"}
 def test_every_path_against_oracle(mq, oracle, cuda_device, path, q):
     """Each kernel, forced, on odd shapes: tail blocks (K % 32), row tails
     (N % 16, N % 128), activation counts around every tile edge."""
-    ms = {1: [1, 2, 3, 4, 5, 9], 4: [1, 2, 4, 5, 8, 9, 16, 17, 32, 33], 2: [1, 7, 128, 129, 300]}[path]
+    ms = {1: [1, 2, 3, 4, 5, 9], 3: [1, 2, 3, 4, 5, 9], 4: [1, 2, 4, 5, 8, 9, 16, 17, 32, 33],
+          2: [1, 7, 128, 129, 300]}[path]
     for rows, cols in [(300, 4097), (136, 320), (1000, 96)]:
         for m in ms:
             s, x, y_ref, bound = _llama_case(mq, oracle, q, rows, cols, m, seed=rows * 7 + m + path)
