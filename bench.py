@@ -207,15 +207,15 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     else:
         linear = lib.mq_linear
 
-    def step(stream_handle, events=None, s=0):
-        for j, (h, x, m, k, y, n) in enumerate(calls):
-            if events is not None:
-                record_external(events[s][j], stream_handle)
+    def run_calls(stream_handle, idx):
+        for j in idx:
+            h, x, m, k, y, n = calls[j]
             rc = linear(h, x, m, k, None, y, n, stream_handle)
             if rc:
                 raise RuntimeError(mq._lib.last_error())
-        if events is not None:
-            record_external(events[s][-1], stream_handle)
+
+    def step(stream_handle):
+        run_calls(stream_handle, range(len(calls)))
 
     def barrier():
         if world > 1:
@@ -224,20 +224,20 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     # The timed region replays a CUDA graph holding exactly K steps, captured on
     # a dedicated stream after eager warm-up on that stream (so per-stream
-    # scratch already exists). External event nodes between the products give
-    # each product's device time inside the timed region.
+    # scratch already exists). Nothing sits between the products inside the
+    # graph, so consecutive kernels overlap through programmatic dependent
+    # launch as they do in an application's stream.
     cap = torch.cuda.Stream(dev)
     cap_h = C.c_void_p(cap.cuda_stream)
     with torch.cuda.stream(cap):
         for _ in range(args.warmup):
             step(cap_h)
     barrier()
-    ev = [[new_event() for _ in range(len(calls) + 1)] for _ in range(args.steps)]
     graph = torch.cuda.CUDAGraph()
     launches0 = lib.mq_kernel_launches()
     with torch.cuda.graph(graph, stream=cap):
         for s in range(args.steps):
-            step(cap_h, ev, s)
+            step(cap_h)
     launches = lib.mq_kernel_launches() - launches0  # kernels inside the timed graph
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(cap):  # replay, and both timing events, on the capture stream
@@ -256,18 +256,39 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         ms = float(t.item())
     ms_per_step = ms / args.steps
 
-    # Per-product device time, grouped by kernel class (type, M).
-    per_class: dict[str, float] = {}
+    # Device time per kernel class (type, M): a graph per class holding the
+    # class's products (gate, up, down) K times back to back, timed with CUDA
+    # events on the capture stream; the same calls as in the step, so the
+    # kernels overlap the same way. ms = one pass over the class's products.
+    cls_idx: dict[str, list[int]] = {}
     cls_bytes: dict[str, int] = {}
-    cls_first: dict[str, int] = {}
-    cls_count: dict[str, int] = {}
     for j, (q, m, name, n, k) in enumerate(prods):
         c = f"linear_{TNAME[q]}_m{m}"
-        cls_first.setdefault(c, j)
-        cls_count[c] = cls_count.get(c, 0) + 1
+        cls_idx.setdefault(c, []).append(j)
         cls_bytes[c] = cls_bytes.get(c, 0) + algo_bytes(q, n, k, m)
-        per_class[c] = per_class.get(c, 0.0) + sum(elapsed_ms(ev[s][j], ev[s][j + 1]) for s in range(args.steps))
-    class_ms = {c: v / args.steps for c, v in per_class.items()}
+    cls_first = {c: idx[0] for c, idx in cls_idx.items()}
+    cls_count = {c: len(idx) for c, idx in cls_idx.items()}
+    class_ms: dict[str, float] = {}
+    for c, idx in cls_idx.items():
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap):
+            for _ in range(args.steps):
+                run_calls(cap_h, idx)
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(cap):
+            g.replay()
+            barrier()
+            c0.record(cap)
+            g.replay()
+            c1.record(cap)
+            barrier()
+        cms = c0.elapsed_time(c1) / args.steps
+        if world > 1:
+            t = torch.tensor([cms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            cms = float(t.item())
+        class_ms[c] = cms
+        del g
     dominant = max(class_ms, key=class_ms.get)
     j = cls_first[dominant]
     q, m, _, n, k = prods[j]
@@ -357,33 +378,6 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         comm.close()
     if world > 1:
         dist.destroy_process_group()
-
-
-def new_event():
-    from cuda.bindings import runtime as cudart
-
-    err, ev = cudart.cudaEventCreate()
-    if err != cudart.cudaError_t.cudaSuccess:
-        raise RuntimeError(f"cudaEventCreate: {err}")
-    return ev
-
-
-def record_external(ev, stream_handle) -> None:
-    """Event record node usable for timing inside a captured graph."""
-    from cuda.bindings import runtime as cudart
-
-    (err,) = cudart.cudaEventRecordWithFlags(ev, stream_handle.value, cudart.cudaEventRecordExternal)
-    if err != cudart.cudaError_t.cudaSuccess:
-        raise RuntimeError(f"cudaEventRecordWithFlags: {err}")
-
-
-def elapsed_ms(a, b) -> float:
-    from cuda.bindings import runtime as cudart
-
-    err, ms = cudart.cudaEventElapsedTime(a, b)
-    if err != cudart.cudaError_t.cudaSuccess:
-        raise RuntimeError(f"cudaEventElapsedTime: {err}")
-    return ms
 
 
 def _launches_for(lib, linear, call, sh, torch) -> int:

@@ -411,7 +411,7 @@ int run_sdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const floa
 namespace {
 
 template <int QT, int MC>
-cudaError_t launch_i8dec_t(const CUtensorMap &tx, const I8Args &a, int grid, cudaStream_t s) {
+cudaError_t launch_i8dec_t(const I8Args &a, int grid, cudaStream_t s) {
   using L = I8Cfg<QT, MC>;
   static bool configured = false;
   if (!configured) {
@@ -419,16 +419,16 @@ cudaError_t launch_i8dec_t(const CUtensorMap &tx, const I8Args &a, int grid, cud
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  const cudaError_t e = launch_pdl(i8dec_kernel<QT, MC>, dim3(grid), dim3(kI8Threads), L::kAlloc, s, tx, a);
+  const cudaError_t e = launch_pdl(i8dec_kernel<QT, MC>, dim3(grid), dim3(kI8Threads), L::kAlloc, s, a);
   count_launch();
   return e;
 }
 
 template <int QT>
-cudaError_t launch_i8dec_q(const CUtensorMap &tx, const I8Args &a, int grid, int mc, cudaStream_t s) {
-  if (mc == 1) return launch_i8dec_t<QT, 1>(tx, a, grid, s);
-  if (mc == 2) return launch_i8dec_t<QT, 2>(tx, a, grid, s);
-  return launch_i8dec_t<QT, 4>(tx, a, grid, s);
+cudaError_t launch_i8dec_q(const I8Args &a, int grid, int mc, cudaStream_t s) {
+  if (mc == 1) return launch_i8dec_t<QT, 1>(a, grid, s);
+  if (mc == 2) return launch_i8dec_t<QT, 2>(a, grid, s);
+  return launch_i8dec_t<QT, 4>(a, grid, s);
 }
 
 }  // namespace
@@ -457,36 +457,16 @@ int run_i8dec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
   for (int i0 = 0; i0 < m; i0 += 4) {
     const int mm = std::min(4, m - i0);
     const int mc = mm == 1 ? 1 : (mm == 2 ? 2 : 4);
-    // The activation slices are read by TMA straight from x when its base and
-    // row stride are 16-byte aligned; otherwise x is first copied to an
-    // aligned scratch.
-    const float *xs = x + (int64_t)i0 * ldx;
-    int64_t ldxs = ldx;
-    const bool copy = (reinterpret_cast<uintptr_t>(xs) & 15) != 0 || (ldx & 3) != 0;
-    const int64_t ldc = ((int64_t)w.cols + 3) & ~int64_t(3);
     const size_t pbytes = (size_t)plan.grid * 2 * kI8Rows * mc * 4;
-    const size_t cbytes = copy ? (size_t)mm * ldc * 4 : 0;
     void *ws = nullptr;
-    if ((rc = workspace_for(wt->device, s, pbytes + cbytes + 1024, &ws))) return rc;
-    uint8_t *base = static_cast<uint8_t *>(ws);
-    if (copy) {
-      float *xc = reinterpret_cast<float *>(base + ((pbytes + 255) & ~size_t(255)));
-      MQ_CUDA(cudaMemcpy2DAsync(xc, (size_t)ldc * 4, xs, (size_t)ldx * 4, (size_t)w.cols * 4, (size_t)mm,
-                                cudaMemcpyDeviceToDevice, s));
-      xs = xc;
-      ldxs = ldc;
-    }
-    CUtensorMap tx;
-    if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xs, mm, w.cols, ldxs, 256, mc,
-                        CU_TENSOR_MAP_SWIZZLE_NONE)))
-      return rc;
-    I8Args a{w, mm, bias, y + (int64_t)i0 * ldy, ldy, reinterpret_cast<float *>(base), tickets, plan.steps,
-             plan.tiles, err_dev, 0};
+    if ((rc = workspace_for(wt->device, s, pbytes + 1024, &ws))) return rc;
+    I8Args a{w, mm, x + (int64_t)i0 * ldx, ldx, bias, y + (int64_t)i0 * ldy, ldy, static_cast<float *>(ws), tickets,
+             plan.steps, plan.tiles, err_dev, 0};
     cudaError_t e;
     switch (w.qtype) {
-    case MQ_Q8_0: e = launch_i8dec_q<MQ_Q8_0>(tx, a, plan.grid, mc, s); break;
-    case MQ_Q4_0: e = launch_i8dec_q<MQ_Q4_0>(tx, a, plan.grid, mc, s); break;
-    default: e = launch_i8dec_q<MQ_Q4_1>(tx, a, plan.grid, mc, s); break;
+    case MQ_Q8_0: e = launch_i8dec_q<MQ_Q8_0>(a, plan.grid, mc, s); break;
+    case MQ_Q4_0: e = launch_i8dec_q<MQ_Q4_0>(a, plan.grid, mc, s); break;
+    default: e = launch_i8dec_q<MQ_Q4_1>(a, plan.grid, mc, s); break;
     }
     if (e != cudaSuccess) return cuda_fail(e, "int8 decode launch");
   }

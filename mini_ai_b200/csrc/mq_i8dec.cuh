@@ -22,18 +22,23 @@
 // up to accumulation-order rounding.
 //
 // Data flow per (128-row tile, 8-block step):
-//   weight chunk (packed codes, scales, mins): one bulk copy into the packed
-//   ring and one into the scale ring; a TMA load of the step's activation slice [256 K x
-//   rows] lands in the same scale stage, and prep warps turn it into the limb
-//   tile (B operand, 128-byte-swizzled K-major layout) and a header (2^-e and
-//   the integer block sums of X per activation row) in that stage;
+//   weight chunk (packed codes, fp16 scales, Q4_1 mins; consecutive in
+//   memory): one bulk copy into the chunk ring;
+//   prep warps: the step's activations (plain loads: they stay in L2, and
+//   keeping them off the TMA engine keeps them from queueing behind the
+//   weight copies) -> limb tile (B operand, 128-byte-swizzled K-major) in
+//   the tile ring and a header (2^-e and the integer block sums of X per
+//   activation row) in the step's drain slot;
 //   unpacker warps: packed bytes -> int8/uint8 codes in TMEM (tcgen05.st),
 //   one 64-column A slot per step (no conversion for Q8_0: the codes are
-//   moved as they are; Q4_x: two logic ops per 8 nibbles);
-//   four issuer threads: 2 MMAs each per step (A from TMEM, B from shared
-//   memory), each into its own 16-column D slot, one commit each per step;
+//   moved as they are; Q4_x: two logic ops per 8 nibbles); they also copy
+//   the row's scales into the drain slot and release the chunk at once;
+//   issuer threads, taking the steps in turn: 8 MMAs per step (A from TMEM,
+//   B from shared memory) into the step's D slot, one commit per step;
 //   drainer warps: tcgen05.ld of the step's D slots, limb combine, block
 //   scales, accumulate; at the end of a tile: bias, store or stream-K partial.
+// Every ring is released as soon as its data has moved on, so the weight
+// stream is throttled only by the chunk ring and the A slots.
 //
 // K order inside a block. The A columns of a block follow the device weight
 // layout: column 2t + h holds, in its four bytes p = 0..3,
@@ -44,12 +49,12 @@
 // Persistent stream-K over the tile-major step space, as the other decode
 // kernels: a tile whose K loop is split across CTAs is completed by the last
 // contributor from at most two partial slots per CTA (deterministic order).
-// Warp roles (22 warps): warp 0 bulk copies of the packed codes; warp 21 bulk
-// copies of the scales and TMA loads of the activation slices; warps 1, 2, 3
-// and 20 MMA issue, one thread each, two of every step's 8 blocks each
-// (issuing a tcgen05.mma occupies its thread for about 80 ns, measured on
-// B200, so one issuer would add ~0.6 us to every step's latency); warp 1 also
-// allocates the TMEM; warps 4..7 prep (limb tiles), taking the steps in turn;
+// Warp roles (21 warps): warp 0 bulk copies of the weight chunks; warps 1, 2, 3
+// and 20 MMA issue, one thread each, taking the steps in turn (issuing a
+// tcgen05.mma occupies its thread for about 80 ns, measured on B200, so one
+// issuer could not keep up with HBM); warp 1 also
+// allocates the TMEM; warps 4..7 prep (limb tiles from the L2-resident
+// activations, one step ahead), taking the steps in turn;
 // warps 8..15 unpackers (two per TMEM lane quarter, one quad of 4 blocks
 // each); warps 16..19 drainers (one per lane quarter). Every wait is
 // bounded in time; a timeout raises the CTA abort flag and the host-visible
@@ -71,8 +76,8 @@
 namespace mq {
 
 constexpr int kI8Rows = 128;
-constexpr int kI8Warps = 22;
-constexpr int kI8Issuers = 4;       // MMA issue threads (warps 1, 2, 3, 20), 2 of a step's 8 blocks each
+constexpr int kI8Warps = 21;
+constexpr int kI8Issuers = 4;       // MMA issue threads at most (warps 1, 2, 3, 20), taking the steps in turn
 constexpr int kI8Preps = 4;         // prep warps (4..7): step s is built by warp 4 + s % 4
 constexpr int kI8Threads = kI8Warps * 32;
 constexpr int kI8MaxM = 5;          // activation rows per launch: 3 limbs x 5 rows <= N = 16
@@ -87,6 +92,8 @@ constexpr uint64_t kI8DrainNs = 20000000ull;
 struct I8Args {
   WeightView w;
   int m;                 // activation rows (<= MC)
+  const float *x;        // [m][ldx] activations
+  int64_t ldx;
   const float *bias;
   float *y;
   int64_t ldy;
@@ -100,34 +107,51 @@ struct I8Args {
 
 template <int QT, int MC>
 struct I8Cfg {
-  static constexpr int kPkBytes = step_pk_bytes(QT);            // packed codes of a step
-  static constexpr int kScBytes = step_sc_bytes(QT);            // scales (+ mins)
-  // scale stage: B tile | header | scales (+ mins) | activation slice [MC][256] f32
-  static constexpr int kSbHdr = kI8BTile;
-  static constexpr int kSbSc = kI8BTile + 512;
-  static constexpr int kSbX = kSbSc + kScBytes;
-  static constexpr int kXBytes = MC * 256 * 4;
-  static constexpr int kSbBytes = ((kSbX + kXBytes) + 1023) / 1024 * 1024;
-  static constexpr int SS = 8;                                  // scale / B stages
-  static constexpr int kPsFit = (220 * 1024 - SS * kSbBytes) / kPkBytes;
-  static constexpr int PS = kPsFit < 8 ? kPsFit : 8;            // packed stages
-  static constexpr int NA = 2;                                  // A slots in TMEM (64 columns each)
-  static constexpr int ND = 3;                                  // D slots in TMEM (128 columns each)
-  static constexpr int kACols = 64, kDCols = 8 * kI8N, kDOff = NA * kACols;
+  static constexpr int kPkBytes = step_pk_bytes(QT);   // packed codes of a step
+  static constexpr int kScBytes = step_sc_bytes(QT);   // fp16 scales (+ Q4_1 mins) of a step
+  static constexpr int kChunk = kPkBytes + kScBytes;   // one weight chunk: one bulk copy per step
+  static constexpr int kDrBytes = kScBytes + 512;      // drain slot: scales (+ mins) | header
+  static constexpr int kDrHdr = kScBytes;
+  static constexpr int NB = kI8Preps;                  // limb tiles (4 KB each)
+  static constexpr int DS = 8;                         // drain slots
+  // Blocks per D region: with 3 MC limb rows <= 8, block 2i + 1's limbs sit in
+  // B rows 8.. and block 2i's in rows 0.. (each with zeros in the other
+  // half), so the pair's two MMAs accumulate into one 16-column region and a
+  // step needs half the D columns.
+  static constexpr int G = 3 * MC <= 8 ? 2 : 1;
+  static constexpr int kRowOff = 16 / G;               // B row offset between the blocks of a pair
+  // TMEM: the unpack -> MMA -> completion round trip (~1.1 us measured) gates
+  // the A slots, the MMA -> drain round trip (~1 us) the D slots.
+  static constexpr int NA = G == 2 ? 4 : 2;            // A slots in TMEM (64 columns each)
+  static constexpr int kACols = 64, kDCols = 8 * kI8N / G, kDOff = NA * kACols;
+  static constexpr int ND = (512 - kDOff) / kDCols;    // D slots in TMEM
+  // Issuers take the steps in turn (each issues a whole step: tcgen05.mma
+  // costs its thread ~80 ns, so several steps must be in issue at once). A
+  // parity wait is sound only while the awaited phase is the barrier's
+  // current or immediately preceding one; with I issuers that holds when every
+  // per-step ring (A slots, tiles, commits) is a multiple of I, so that one
+  // issuer owns all phases of a barrier, and ND >= I (the issuer of step s
+  // waited for the drain of s - I - ND before it waits for s - ND).
+  static constexpr int I = ND >= 4 ? 4 : (ND >= 2 ? 2 : 1);
+  static_assert(NA % I == 0 && NB % I == 0 && kI8Done % I == 0 && ND >= I, "issuer ownership of the rings");
   static_assert(kDOff + ND * kDCols <= 512, "TMEM budget");
-  static constexpr int kPkOff = 0;
-  static constexpr int kSbOff = kPkOff + PS * kPkBytes;
-  static constexpr int kBarOff = kSbOff + SS * kSbBytes;
-  static constexpr int kNumBars = 2 * PS + 3 * SS + NA + ND + kI8Done + kI8Issuers;
-  static_assert(SS % kI8Preps == 0, "a prep warp owns every phase of its stages");
+  static_assert(kI8Preps <= DS && kI8Preps <= kI8Done && DS % kI8Preps == 0, "ring depths (see the waits)");
+  static constexpr int kBOff = 0;                               // 1 KB aligned (128-byte swizzle atoms)
+  static constexpr int kDrOff = kBOff + NB * kI8BTile;
+  static constexpr int kPkOff = kDrOff + DS * kDrBytes;         // 16-byte aligned bulk destinations
+  static constexpr int kPsFit = (222 * 1024 - kPkOff) / kChunk;
+  static constexpr int PS = kPsFit < 12 ? kPsFit : 12;          // weight chunks in flight
+  static constexpr int kBarOff = kPkOff + PS * kChunk;
+  static constexpr int kNumBars = 2 * PS + NB + 2 * DS + NA + ND + kI8Done + kI8Issuers;
   static constexpr int kBytes = kBarOff + 8 * kNumBars + 16;
   static constexpr int kAlloc = kBytes + 1024;
   static_assert(PS >= 3 && kAlloc <= 227 * 1024, "shared memory budget");
-  // D columns the drainers read per block (3 limbs per activation row) and
-  // blocks per batch of TMEM loads (32 registers a batch).
-  static constexpr int NCOL = MC <= 1 ? 4 : (MC <= 2 ? 8 : 16);
+  static_assert(kChunk % 16 == 0 && kDrBytes % 16 == 0, "copy alignment");
+  // D columns the drainers read per region and regions per batch of TMEM
+  // loads (32 registers a batch).
+  static constexpr int NCOL = G == 2 ? 16 : (MC <= 1 ? 4 : (MC <= 2 ? 8 : 16));
   static constexpr int BB = 32 / NCOL;
-  static_assert(3 * MC <= NCOL || NCOL == 16, "limb columns");
+  static_assert(3 * MC <= NCOL, "limb columns");
   static_assert(MC <= kI8MaxM, "activation rows");
 };
 
@@ -138,13 +162,14 @@ __host__ __device__ constexpr uint32_t idesc_i8_s32(int M, int N, bool a_signed)
          ((uint32_t)(M >> 4) << 24);
 }
 
-// D[tmem] = A[tmem] x B[smem]^T, kind::i8 (no accumulation: each block has its own slot).
-__device__ __forceinline__ void umma_i8_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc) {
+// D[tmem] (+)= A[tmem] x B[smem]^T, kind::i8.
+__device__ __forceinline__ void umma_i8_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, 0, 0;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "r"(tmem_a), "l"(bdesc), "r"(idesc)
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -178,17 +203,17 @@ __host__ __device__ inline int i8_slot_elem(int qtype, int c, int p) {
 }
 
 template <int QT, int MC>
-__global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const __grid_constant__ CUtensorMap tm_x, const I8Args a) {
+__global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
   using L = I8Cfg<QT, MC>;
-  constexpr int PS = L::PS, SS = L::SS, NA = L::NA, ND = L::ND, NCOL = L::NCOL, BB = L::BB;
+  constexpr int PS = L::PS, NB = L::NB, DS = L::DS, NA = L::NA, ND = L::ND, NCOL = L::NCOL, BB = L::BB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::kBarOff);
-  uint64_t *pk_full = bars, *pk_empty = pk_full + PS;
-  // sbx_full: scales + activation slice landed (TMA); sb_full: B tile and header built (prep warps)
-  uint64_t *sb_full = pk_empty + PS, *sb_empty = sb_full + SS, *sbx_full = sb_empty + SS;
-  // a_full: per A slot; d_empty: per D slot; done: commit ring (4 commits a step); fin: per issuer
-  uint64_t *a_full = sbx_full + SS, *d_empty = a_full + NA, *done = d_empty + ND, *fin = done + kI8Done;
+  uint64_t *pk_full = bars, *pk_empty = pk_full + PS;   // weight chunks: bulk copy / unpackers
+  uint64_t *b_full = pk_empty + PS;                     // limb tiles built (prep); reuse after the MMAs (done)
+  uint64_t *dr_full = b_full + NB, *dr_empty = dr_full + DS;  // drain slots: unpackers + prep / drainers
+  uint64_t *a_full = dr_empty + DS, *d_empty = a_full + NA;   // TMEM A slots (unpackers), D slots (drainers)
+  uint64_t *done = d_empty + ND, *fin = done + kI8Done;       // MMA commits (4 a step), per-issuer final commit
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::kNumBars);
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
   __shared__ int s_last;
@@ -200,11 +225,11 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const __grid_const
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < PS; ++i) sm100::mbar_init(&pk_full[i], 1), sm100::mbar_init(&pk_empty[i], 8);
-    for (int i = 0; i < SS; ++i)
-      sm100::mbar_init(&sb_full[i], 1), sm100::mbar_init(&sb_empty[i], 4), sm100::mbar_init(&sbx_full[i], 1);
+    for (int i = 0; i < NB; ++i) sm100::mbar_init(&b_full[i], 1);
+    for (int i = 0; i < DS; ++i) sm100::mbar_init(&dr_full[i], 5), sm100::mbar_init(&dr_empty[i], 4);
     for (int i = 0; i < NA; ++i) sm100::mbar_init(&a_full[i], 8);
     for (int i = 0; i < ND; ++i) sm100::mbar_init(&d_empty[i], 4);
-    for (int i = 0; i < kI8Done; ++i) sm100::mbar_init(&done[i], kI8Issuers);
+    for (int i = 0; i < kI8Done; ++i) sm100::mbar_init(&done[i], 1);
     for (int i = 0; i < kI8Issuers; ++i) sm100::mbar_init(&fin[i], 1);
     *abort = 0;
     sm100::fence_mbar_init();
@@ -219,53 +244,27 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const __grid_const
   const uint32_t tmem = *tmem_slot;
   if (threadIdx.x == 0) sm100::griddep_launch_dependents();
 
+  // Parity waits are sound only while the awaited phase is the barrier's
+  // current or immediately preceding one. Every ring below is filled and
+  // drained in step order, except that the prep warps take steps in turn:
+  // the tile ring has one stage per prep warp, and a prep warp's waits on the
+  // shared rings (done, dr_empty) for step s come after its own waits for
+  // step s - kI8Preps, which covered the previous phase (kI8Preps <= DS, kDone).
   if (warp == 0) {
-    if (lane == 0) {  // --------------------------------------- bulk copies: packed codes
-      // (An L2 bulk prefetch ahead of this ring measured slower: it goes
-      // through the same per-SM TMA engine and delays the ring's own copies.)
+    if (lane == 0) {  // --------------------------------------- weight chunks: codes + scales, one bulk copy a step
       int issued = 0;
       for (int ls = 0; ls < nsteps; ++ls) {
         const int g = g0 + ls, i = ls % PS;
         if (ls >= PS &&
             !sm100::mbar_wait_sleep(&pk_empty[i], ((uint32_t)(ls / PS) & 1u) ^ 1u, a.err, abort, kI8WaitNs))
           break;
-        sm100::mbar_arrive_expect_tx(&pk_full[i], L::kPkBytes);
-        sm100::bulk_load(smem + L::kPkOff + i * L::kPkBytes, chunk_ptr(a.w, g / S, g % S), L::kPkBytes, &pk_full[i]);
+        sm100::mbar_arrive_expect_tx(&pk_full[i], L::kChunk);
+        sm100::bulk_load(smem + L::kPkOff + i * L::kChunk, chunk_ptr(a.w, g / S, g % S), L::kChunk, &pk_full[i]);
         issued = ls + 1;
       }
       // No copy may still be landing when the CTA exits.
       for (int p = issued - PS < 0 ? 0 : issued - PS; p < issued; ++p)
         sm100::mbar_wait(&pk_full[p % PS], (uint32_t)(p / PS) & 1u, nullptr, nullptr, kI8DrainNs);
-    }
-  } else if (warp == 21) {
-    if (lane == 0) {  // --------------------------------------- bulk copies: scales (+ mins), activation slices
-      sm100::prefetch_tmap(&tm_x);
-      auto issue_sc = [&](int ls) {
-        const int g = g0 + ls, i = ls % SS;
-        sm100::mbar_arrive_expect_tx(&sbx_full[i], L::kScBytes + L::kXBytes);
-        sm100::bulk_load(smem + L::kSbOff + i * L::kSbBytes + L::kSbSc, chunk_ptr(a.w, g / S, g % S) + L::kPkBytes,
-                         L::kScBytes, &sbx_full[i]);
-      };
-      auto issue_x = [&](int ls) {  // rows >= m and K past the end read as zeros
-        const int i = ls % SS;
-        sm100::tma_load_2d(smem + L::kSbOff + i * L::kSbBytes + L::kSbX, &tm_x, ((g0 + ls) % S) * 256, 0, &sbx_full[i]);
-      };
-      // The scales are read-only: the first ring's worth streams in while the
-      // previous kernel of the stream (which may produce x) still runs.
-      const int pre = nsteps < SS ? nsteps : SS;
-      for (int ls = 0; ls < pre; ++ls) issue_sc(ls);
-      sm100::griddep_wait();
-      for (int ls = 0; ls < pre; ++ls) issue_x(ls);
-      int issued = pre;
-      for (int ls = pre; ls < nsteps; ++ls) {
-        if (!sm100::mbar_wait_sleep(&sb_empty[ls % SS], ((uint32_t)(ls / SS) & 1u) ^ 1u, a.err, abort, kI8WaitNs))
-          break;
-        issue_sc(ls);
-        issue_x(ls);
-        issued = ls + 1;
-      }
-      for (int p = issued - SS < 0 ? 0 : issued - SS; p < issued; ++p)
-        sm100::mbar_wait(&sbx_full[p % SS], (uint32_t)(p / SS) & 1u, nullptr, nullptr, kI8DrainNs);
     }
   } else if (warp >= 4 && warp < 4 + kI8Preps) {  // ---------- prep: activation slice -> limb tile + header
     // Lane l builds the 4-slot words w = l and l + 32 of each limb row (word
@@ -274,41 +273,67 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const __grid_const
     // even through the fp32 magic 1.5 * 2^23), split into balanced limbs
     // X = l0 + 2^8 l1 + 2^16 l2; the header holds 2^-e and the integer block
     // sums of X. A non-finite value in the slice makes 2^-e NaN, so that row's
-    // outputs become NaN. Rows >= m (zero filled by the TMA load) get zero limbs.
+    // outputs become NaN.
     const int pw = warp - 4;
-    auto word_off = [](int n, int w) {  // byte offset of word w of B row n inside the B tile
+    auto word_off = [](int n, int w) {  // byte offset of word w of B row n inside a limb tile
       const int j = w >> 3, c8 = w & 7;
       const int pos = 32 * (j & 3) + 4 * c8;  // byte inside the slab's 128-byte row
       return (j >> 2) * 2048 + (n >> 3) * 1024 + (n & 7) * 128 + (((pos >> 4) ^ (n & 7)) << 4) + (pos & 15);
     };
-    for (int ls = pw; ls < nsteps; ls += kI8Preps) {
-      const int i = ls % SS;
-      if (!__all_sync(0xffffffffu,
-                      sm100::mbar_wait_sleep(&sbx_full[i], (uint32_t)(ls / SS) & 1u, a.err, abort, kI8WaitNs)))
-        break;
-      uint8_t *stage = smem + L::kSbOff + i * L::kSbBytes;
-      const float *xs = reinterpret_cast<const float *>(stage + L::kSbX);
-      float *inv = reinterpret_cast<float *>(stage + L::kSbHdr + kI8HdrInv);
-      int *sx = reinterpret_cast<int *>(stage + L::kSbHdr + kI8HdrSx);
+    // A lane's 8 values of row t: the slots 4c + p of column c = 2 tt + h hold
+    // the elements 2 tt + {0, 8, 1, 9} + 16 h (Q4_x) or 2 tt + {0, 1, 8, 9} +
+    // 16 h (Q8_0); rows >= m and K past the end read as zeros. The
+    // activations are L2-resident: each prep warp loads its next step's values
+    // while it builds the current one.
+    auto load = [&](int ls, float (&v)[MC][8]) {
+      const int k0 = ((g0 + ls) % S) * 256;
 #pragma unroll
       for (int t = 0; t < MC; ++t) {
-        // slots 4c + p of column c = 2 tt + h hold the elements 2 tt + {0, 8, 1, 9} + 16 h (Q4_x) or
-        // 2 tt + {0, 1, 8, 9} + 16 h (Q8_0): two float2 loads per word
-        float v[8];
+        const bool live = t < a.m;
+        const float *xr = a.x + (int64_t)(live ? t : 0) * a.ldx;
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int w = lane + 32 * u, j = w >> 3, c8 = w & 7;
-          const float *bx = xs + t * 256 + 32 * j + 2 * (c8 >> 1) + 16 * (c8 & 1);
-          const float2 lo = *reinterpret_cast<const float2 *>(bx), hi = *reinterpret_cast<const float2 *>(bx + 8);
-          if constexpr (QT == MQ_Q8_0) {
-            v[4 * u + 0] = lo.x, v[4 * u + 1] = lo.y, v[4 * u + 2] = hi.x, v[4 * u + 3] = hi.y;
-          } else {
-            v[4 * u + 0] = lo.x, v[4 * u + 1] = hi.x, v[4 * u + 2] = lo.y, v[4 * u + 3] = hi.y;
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const int k = k0 + 32 * j + i8_slot_elem(QT, c8, p);
+            v[t][4 * u + p] = (live && k < a.w.cols) ? __ldg(xr + k) : 0.0f;
           }
         }
+      }
+    };
+    sm100::griddep_wait();  // the activations may come from the previous kernel
+    constexpr bool kPf = MC <= 2;  // prefetch the next step's values (register budget: not for 4 rows)
+    float v[MC][8], nv[kPf ? MC : 1][8];
+    if (kPf && pw < nsteps) load(pw, *reinterpret_cast<float(*)[MC][8]>(&nv[0][0]));
+    for (int ls = pw; ls < nsteps; ls += kI8Preps) {
+      const int bi = ls % NB, di = ls % DS;
+      if constexpr (kPf) {
+#pragma unroll
+        for (int t = 0; t < MC; ++t)
+#pragma unroll
+          for (int q = 0; q < 8; ++q) v[t][q] = nv[t][q];
+        if (ls + kI8Preps < nsteps) load(ls + kI8Preps, *reinterpret_cast<float(*)[MC][8]>(&nv[0][0]));
+      } else {
+        load(ls, v);
+      }
+      bool ok = true;
+      if (ls >= NB) {  // the limb tile is free once the MMAs of step ls - NB completed
+        const int pd = ls - NB;
+        ok = ok && sm100::mbar_wait_sleep(&done[pd % kI8Done], (uint32_t)(pd / kI8Done) & 1u, a.err, abort, kI8WaitNs);
+      }
+      if (ls >= DS)
+        ok = ok && sm100::mbar_wait_sleep(&dr_empty[di], ((uint32_t)(ls / DS) & 1u) ^ 1u, a.err, abort, kI8WaitNs);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      uint8_t *tile = smem + L::kBOff + bi * kI8BTile;
+      uint8_t *hdr = smem + L::kDrOff + di * L::kDrBytes + L::kDrHdr;
+      float *inv = reinterpret_cast<float *>(hdr + kI8HdrInv);
+      int *sx = reinterpret_cast<int *>(hdr + kI8HdrSx);
+#pragma unroll
+      for (int t = 0; t < MC; ++t) {
         uint32_t mb = 0u;  // largest |x| bits (integer order = magnitude order, NaN above Inf)
 #pragma unroll
-        for (int q = 0; q < 8; ++q) mb = max(mb, __float_as_uint(v[q]) & 0x7fffffffu);
+        for (int q = 0; q < 8; ++q) mb = max(mb, __float_as_uint(v[t][q]) & 0x7fffffffu);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
         const bool finite = mb < 0x7f800000u;
@@ -319,7 +344,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const __grid_const
         int X[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q)
-          X[q] = finite ? (int)(__float_as_uint(fmaf(v[q], sc, 12582912.0f)) - 0x4B400000u) : 0;
+          X[q] = finite ? (int)(__float_as_uint(fmaf(v[t][q], sc, 12582912.0f)) - 0x4B400000u) : 0;
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int w = lane + 32 * u;
@@ -331,12 +356,16 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const __grid_const
             const int l2 = (x1 - (int)(int8_t)x1) >> 8;
             b0[p] = (uint32_t)xv & 255u, b1[p] = (uint32_t)x1 & 255u, b2[p] = (uint32_t)l2 & 255u;
           }
-          const uint32_t w0 = b0[0] | (b0[1] << 8) | (b0[2] << 16) | (b0[3] << 24);
-          const uint32_t w1 = b1[0] | (b1[1] << 8) | (b1[2] << 16) | (b1[3] << 24);
-          const uint32_t w2 = b2[0] | (b2[1] << 8) | (b2[2] << 16) | (b2[3] << 24);
-          *reinterpret_cast<uint32_t *>(stage + word_off(3 * t + 0, w)) = w0;
-          *reinterpret_cast<uint32_t *>(stage + word_off(3 * t + 1, w)) = w1;
-          *reinterpret_cast<uint32_t *>(stage + word_off(3 * t + 2, w)) = w2;
+          // rows of this word's block; with block pairs, zeros in the partner block's rows
+          const int rb = ((w >> 3) % L::G) * L::kRowOff + 3 * t;
+          *reinterpret_cast<uint32_t *>(tile + word_off(rb + 0, w)) = b0[0] | (b0[1] << 8) | (b0[2] << 16) | (b0[3] << 24);
+          *reinterpret_cast<uint32_t *>(tile + word_off(rb + 1, w)) = b1[0] | (b1[1] << 8) | (b1[2] << 16) | (b1[3] << 24);
+          *reinterpret_cast<uint32_t *>(tile + word_off(rb + 2, w)) = b2[0] | (b2[1] << 8) | (b2[2] << 16) | (b2[3] << 24);
+          if constexpr (L::G == 2) {
+            const int rz = (1 - ((w >> 3) & 1)) * L::kRowOff + 3 * t;
+#pragma unroll
+            for (int l = 0; l < 3; ++l) *reinterpret_cast<uint32_t *>(tile + word_off(rz + l, w)) = 0u;
+          }
         }
         // integer block sums: word w of lane l belongs to block w / 8 = lane / 8 (+ 4)
         int s0 = X[0] + X[1] + X[2] + X[3], s1 = X[4] + X[5] + X[6] + X[7];
@@ -353,27 +382,31 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const __grid_const
       }
       sm100::fence_proxy_async_smem();  // the MMAs read the tile through the async proxy
       __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(&sb_full[i]);
+      if (lane == 0) {
+        sm100::mbar_arrive(&b_full[bi]);
+        sm100::mbar_arrive(&dr_full[di]);
+      }
     }
   } else if ((warp >= 1 && warp <= 3) || warp == 20) {
     const int issuer = warp == 20 ? 3 : warp - 1;
-    if (lane == 0) {  // --------------------------------------- MMA issue: blocks 2 issuer, 2 issuer + 1 of every step
+    if (lane == 0 && issuer < L::I) {  // ------------------------- MMA issue: steps issuer, issuer + I, ...
       constexpr uint32_t idesc = idesc_i8_s32(kI8Rows, kI8N, QT == MQ_Q8_0);
-      for (int ls = 0; ls < nsteps; ++ls) {
+      for (int ls = issuer; ls < nsteps; ls += L::I) {
         bool ok = sm100::mbar_wait(&a_full[ls % NA], (uint32_t)(ls / NA) & 1u, a.err, abort, kI8WaitNs);
-        ok = ok && sm100::mbar_wait(&sb_full[ls % SS], (uint32_t)(ls / SS) & 1u, a.err, abort, kI8WaitNs);
+        ok = ok && sm100::mbar_wait(&b_full[ls % NB], (uint32_t)(ls / NB) & 1u, a.err, abort, kI8WaitNs);
         ok = ok && sm100::mbar_wait(&d_empty[ls % ND], ((uint32_t)(ls / ND) & 1u) ^ 1u, a.err, abort, kI8WaitNs);
         if (!ok) break;
         sm100::tc_fence_after();
         const uint32_t abase = tmem + (uint32_t)((ls % NA) * L::kACols);
         const uint32_t dbase = tmem + (uint32_t)(L::kDOff + (ls % ND) * L::kDCols);
-        const uint64_t bdesc = sm100::umma_desc_sw128(sm100::smem_u32(smem + L::kSbOff + (ls % SS) * L::kSbBytes));
+        const uint64_t bdesc = sm100::umma_desc_sw128(sm100::smem_u32(smem + L::kBOff + (ls % NB) * kI8BTile));
 #pragma unroll
-        for (int jj = 0; jj < 2; ++jj) {
-          // block j: slab j / 4 (2 KB), K offset 32 * (j % 4) bytes inside the 128-byte row
-          const int j = 2 * issuer + jj;
+        for (int j = 0; j < 8; ++j) {
+          // block j: slab j / 4 (2 KB), K offset 32 * (j % 4) bytes inside the 128-byte row; a
+          // block pair of one D region accumulates in issue order
           const uint32_t off = (uint32_t)((j >> 2) * 2048 + (j & 3) * 32);
-          umma_i8_tmem_a(dbase + (uint32_t)(j * kI8N), abase + (uint32_t)(8 * j), bdesc + (off >> 4), idesc);
+          umma_i8_tmem_a(dbase + (uint32_t)((j / L::G) * kI8N), abase + (uint32_t)(8 * j), bdesc + (off >> 4), idesc,
+                         (uint32_t)(j % L::G));
         }
         sm100::umma_commit(&done[ls % kI8Done]);
       }
@@ -388,21 +421,27 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const __grid_const
     const int sw = r & 7;
     const uint32_t lane_base = (uint32_t)(32 * qq) << 16;
     for (int ls = 0; ls < nsteps; ++ls) {
-      const int pi = ls % PS;
+      const int pi = ls % PS, di = ls % DS;
       // tcgen05.st is warp-collective: every wait result is made warp-uniform.
-      bool ok = __all_sync(0xffffffffu,
-                           sm100::mbar_wait_sleep(&pk_full[pi], (uint32_t)(ls / PS) & 1u, a.err, abort, kI8WaitNs));
-      if (ok && ls >= NA) {  // the A slot is free once the MMAs of step ls - NA completed
+      bool ok = sm100::mbar_wait_sleep(&pk_full[pi], (uint32_t)(ls / PS) & 1u, a.err, abort, kI8WaitNs);
+      if (ls >= NA) {  // the A slot is free once the MMAs of step ls - NA completed
         const int pd = ls - NA;
-        ok = __all_sync(0xffffffffu, sm100::mbar_wait_sleep(&done[pd % kI8Done], (uint32_t)(pd / kI8Done) & 1u, a.err,
-                                                            abort, kI8WaitNs));
+        ok = ok && sm100::mbar_wait_sleep(&done[pd % kI8Done], (uint32_t)(pd / kI8Done) & 1u, a.err, abort, kI8WaitNs);
       }
-      if (!ok) break;
-      // The quad's packed bytes go to registers first; the stage is released
-      // before they are converted and stored to TMEM.
+      if (h == 0 && ls >= DS)  // quad-0 warps also move the step's scales into a drain slot
+        ok = ok && sm100::mbar_wait_sleep(&dr_empty[di], ((uint32_t)(ls / DS) & 1u) ^ 1u, a.err, abort, kI8WaitNs);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      const uint8_t *chunk = smem + L::kPkOff + pi * L::kChunk;
+      // The quad's packed bytes (and the row's scales) go to registers first;
+      // the chunk is released before they are converted and stored.
+      uint4 sc4 = make_uint4(0u, 0u, 0u, 0u), mn4 = make_uint4(0u, 0u, 0u, 0u);
+      if (h == 0) {
+        sc4 = *reinterpret_cast<const uint4 *>(chunk + L::kPkBytes + r * 16);
+        if constexpr (QT == MQ_Q4_1) mn4 = *reinterpret_cast<const uint4 *>(chunk + L::kPkBytes + kI8Rows * 16 + r * 16);
+      }
       uint32_t col[32];  // [block j of the quad][8 columns]
       if constexpr (QT == MQ_Q8_0) {
-        const uint8_t *prow = smem + L::kPkOff + pi * L::kPkBytes + h * (kI8Rows * 128) + r * 128;
+        const uint8_t *prow = chunk + h * (kI8Rows * 128) + r * 128;
         uint32_t cw[8][4];
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
@@ -419,7 +458,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const __grid_const
             col[8 * j + 2 * t + 1] = cw[2 * t + (j >> 1)][2 * (j & 1) + 1];
           }
       } else {
-        const uint8_t *prow = smem + L::kPkOff + pi * L::kPkBytes + r * 128;
+        const uint8_t *prow = chunk + r * 128;
         uint4 v4[4];
 #pragma unroll
         for (int t = 0; t < 4; ++t) v4[t] = *reinterpret_cast<const uint4 *>(prow + (((4 * h + t) ^ sw) << 4));
@@ -435,15 +474,20 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const __grid_const
           }
         }
       }
+      if (h == 0) {
+        uint8_t *dr = smem + L::kDrOff + di * L::kDrBytes;
+        *reinterpret_cast<uint4 *>(dr + r * 16) = sc4;
+        if constexpr (QT == MQ_Q4_1) *reinterpret_cast<uint4 *>(dr + kI8Rows * 16 + r * 16) = mn4;
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&dr_full[di]);
+      }
       tmem_st_x32(tmem + lane_base + (uint32_t)((ls % NA) * L::kACols + 32 * h), col);
       tmem_st_wait();
       sm100::tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        sm100::mbar_arrive(&a_full[ls % NA]);
-      }
+      if (lane == 0) sm100::mbar_arrive(&a_full[ls % NA]);
     }
-  } else if (warp >= 16) {  // -------------------------------------- drainers (TMEM lane = tile row)
+  } else if (warp >= 16 && warp < 20) {  // ------------------------- drainers (TMEM lane = tile row)
     sm100::griddep_wait();  // outputs, partial slots and tickets may still be in use by the previous kernel
     const int qq = warp & 3;
     const int r = 32 * qq + lane;
@@ -511,44 +555,45 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const __grid_const
 #pragma unroll
         for (int c = 0; c < MC; ++c) acc[c] = 0.0f;
       }
-      const int si = ls % SS;
+      const int di = ls % DS;
       // Failed waits do not leave the loop: every drainer must run the same
       // sequence of flushes (they synchronise on a named barrier).
-      bool ok = sm100::mbar_wait_sleep(&sb_full[si], (uint32_t)(ls / SS) & 1u, a.err, abort, kI8WaitNs);
+      bool ok = sm100::mbar_wait_sleep(&dr_full[di], (uint32_t)(ls / DS) & 1u, a.err, abort, kI8WaitNs);
       ok = ok && sm100::mbar_wait_sleep(&done[ls % kI8Done], (uint32_t)(ls / kI8Done) & 1u, a.err, abort, kI8WaitNs);
       ok = __all_sync(0xffffffffu, ok);
       sm100::tc_fence_after();
-      const uint8_t *sb = smem + L::kSbOff + si * L::kSbBytes;
-      const uint4 dq = *reinterpret_cast<const uint4 *>(sb + L::kSbSc + r * 16);
+      const uint8_t *dr = smem + L::kDrOff + di * L::kDrBytes;
+      const uint4 dq = *reinterpret_cast<const uint4 *>(dr + r * 16);
       uint4 mq4 = make_uint4(0u, 0u, 0u, 0u);
-      if constexpr (QT == MQ_Q4_1) mq4 = *reinterpret_cast<const uint4 *>(sb + L::kSbSc + kI8Rows * 16 + r * 16);
+      if constexpr (QT == MQ_Q4_1) mq4 = *reinterpret_cast<const uint4 *>(dr + kI8Rows * 16 + r * 16);
       const uint32_t dw[4] = {dq.x, dq.y, dq.z, dq.w};
       const uint32_t mw[4] = {mq4.x, mq4.y, mq4.z, mq4.w};
-      const float *inv = reinterpret_cast<const float *>(sb + L::kSbHdr + kI8HdrInv);
-      const int *sx = reinterpret_cast<const int *>(sb + L::kSbHdr + kI8HdrSx);
+      const float *inv = reinterpret_cast<const float *>(dr + L::kDrHdr + kI8HdrInv);
+      const int *sx = reinterpret_cast<const int *>(dr + L::kDrHdr + kI8HdrSx);
       const uint32_t dbase = tmem + lane_base + (uint32_t)(L::kDOff + (ls % ND) * L::kDCols);
       float st[MC];  // this step's sum, in the step's activation scale
 #pragma unroll
       for (int c = 0; c < MC; ++c) st[c] = 0.0f;
+      constexpr int kRegions = 8 / L::G;
 #pragma unroll
-      for (int b0 = 0; b0 < 8; b0 += BB) {
+      for (int r0 = 0; r0 < kRegions; r0 += BB) {
         uint32_t v[BB * NCOL];
         if (ok) {
 #pragma unroll
-          for (int jb = 0; jb < BB; ++jb) tmem_ld_cols<NCOL>(dbase + (uint32_t)((b0 + jb) * kI8N), &v[jb * NCOL]);
+          for (int rb = 0; rb < BB; ++rb) tmem_ld_cols<NCOL>(dbase + (uint32_t)((r0 + rb) * kI8N), &v[rb * NCOL]);
           sm100::tmem_ld_wait();
         } else {
 #pragma unroll
           for (int c = 0; c < BB * NCOL; ++c) v[c] = 0u;
         }
-        if (b0 + BB == 8) {  // the D slot is released before the last batch's arithmetic
+        if (r0 + BB == kRegions) {  // the D slot is released before the last batch's arithmetic
           sm100::tc_fence_before();
           __syncwarp();
           if (lane == 0) sm100::mbar_arrive(&d_empty[ls % ND]);
         }
 #pragma unroll
-        for (int jb = 0; jb < BB; ++jb) {
-          const int j = b0 + jb;
+        for (int jb = 0; jb < BB * L::G; ++jb) {
+          const int j = r0 * L::G + jb;
           const __half2 d2 = *reinterpret_cast<const __half2 *>(&dw[j >> 1]);
           const float d = (j & 1) ? __high2float(d2) : __low2float(d2);
           float mn = 0.0f;
@@ -556,7 +601,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const __grid_const
             const __half2 m2 = *reinterpret_cast<const __half2 *>(&mw[j >> 1]);
             mn = (j & 1) ? __high2float(m2) : __low2float(m2);
           }
-          const uint32_t *vb = &v[jb * NCOL];
+          const uint32_t *vb = &v[(jb / L::G) * NCOL + (jb % L::G) * L::kRowOff];
 #pragma unroll
           for (int c = 0; c < MC; ++c) {
             const int l0 = (int)vb[3 * c], l1 = (int)vb[3 * c + 1], l2 = (int)vb[3 * c + 2];
@@ -579,7 +624,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const __grid_const
 #pragma unroll
       for (int c = 0; c < MC; ++c) acc[c] = fmaf(st[c], inv[c], acc[c]);
       __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(&sb_empty[si]);
+      if (lane == 0) sm100::mbar_arrive(&dr_empty[di]);
     }
     if (cur >= 0) flush(cur);
   }
