@@ -11,6 +11,10 @@ finds its weights in L2.
 
 Metric: GB/s of algorithmic bytes, N*ceil(K/32)*block_bytes + 4*M*K + 4*M*N
 per product, over the whole step.
+
+``--workload prefill_ragged_q8_0``: the ragged prefill GEMM (Q8_0 W 11008x4096
+and 4096x11008, 8 requests of 1..512 rows packed to M = 1456) in TFLOP/s of
+2*M*N*K, against the measured dense bf16 peak.
   value : device time, weights and activations resident in HBM;
   e2e   : through the public API with host buffers: every product copies its
           activations from pinned host memory and its outputs back inside the
@@ -50,19 +54,43 @@ Q4_0, Q4_1, Q8_0 = 2, 3, 8
 BLOCK_BYTES = {Q8_0: 34, Q4_0: 18, Q4_1: 20}
 TNAME = {Q8_0: "q8_0", Q4_0: "q4_0", Q4_1: "q4_1"}
 METRIC = "quantized linear GB/s & % HBM peak (decode), TFLOP/s (prefill); tokens/s at 1/2/4/8 GPU"
-UNIT = "GB/s"
 
 WORKLOADS = {
+    # decode GEMVs (the default, the configuration the metric is quoted on): GB/s of algorithmic bytes
     "llama3_8b_ffn_decode": {
         "qtypes": (Q4_0, Q4_1),
         "ms": (1, 4, 16),
         "mats": (("gate", 14336, 4096), ("up", 14336, 4096), ("down", 4096, 14336)),
+        "unit": "GB/s",
+        "desc": "gate/up 14336x4096, down 4096x14336; Q4_0, Q4_1; M = 1, 4, 16",
+        "l2": "inputs larger than L2: 627 MB of distinct weights per GPU per step",
+        "cpu_rows": None,
+    },
+    # ragged prefill GEMM: 8 requests of {1,7,33,64,128,200,511,512} rows (M = 1456) packed
+    # contiguously, Q8_0 W 11008x4096 and 4096x11008: TFLOP/s of 2*M*N*K
+    "prefill_ragged_q8_0": {
+        "qtypes": (Q8_0,),
+        "ms": (1456,),
+        "mats": (("w_up", 11008, 4096), ("w_down", 4096, 11008)),
+        "unit": "TFLOP/s",
+        "desc": "Q8_0 11008x4096 and 4096x11008; 8 ragged requests, M = 1456",
+        "l2": "every product streams 47.9 MB of weights and a 23.9 MB (or 64 MB) activation block",
+        "cpu_rows": 8,  # the CPU reference runs prefill row by row: a bounded sample of rows is timed
     },
 }
 
 
 def algo_bytes(q: int, n: int, k: int, m: int) -> int:
     return n * ((k + 31) // 32) * BLOCK_BYTES[q] + 4 * m * k + 4 * m * n
+
+
+def algo_work(wl: dict, q: int, n: int, k: int, m: int) -> float:
+    """The metric's unit of work for one product: bytes (GB/s) or flops (TFLOP/s)."""
+    return 2.0 * m * n * k if wl["unit"] == "TFLOP/s" else algo_bytes(q, n, k, m)
+
+
+def work_rate(wl: dict, work: float, seconds: float) -> float:
+    return work / seconds / (1e12 if wl["unit"] == "TFLOP/s" else 1e9)
 
 
 def products(wl: dict):
@@ -79,12 +107,14 @@ def select(prods, only: str | None):
     return [p for p in prods if p[0] == q and p[1] == int(m)]
 
 
-def peaks() -> tuple[float, str]:
+def peaks(unit: str = "GB/s") -> tuple[float, str]:
+    """HBM GB/s or dense bf16 TFLOP/s (burst) measured on this pool, else the fallback figures."""
     p = ROOT / "MEASURED_PEAKS.json"
+    key, fallback = ("bf16_tflops", 1590.0) if unit == "TFLOP/s" else ("hbm_gbs", 6650.0)
     try:
-        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        return float(json.loads(p.read_text())[key]), "measured"
     except Exception:
-        return 6650.0, "fallback"
+        return fallback, "fallback"
 
 
 # ---------------------------------------------------------------------------
@@ -198,7 +228,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     calls = [(handles[i].handle, xs[(m, k)].data_ptr(), m, k, ys[(m, n)].data_ptr(), n * world)
              for i, (q, m, name, n, k) in enumerate(prods)]
     # whole-job algorithmic bytes: every rank's shard product (its weights, x, its output slice)
-    bytes_per_step = sum(world * algo_bytes(q, n, k, m) for (q, m, _, n, k) in prods)
+    work_per_step = sum(world * algo_work(wl, q, n, k, m) for (q, m, _, n, k) in prods)
     if world > 1:
         gather = lib.mq_linear_sharded_allgather
 
@@ -265,7 +295,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     for j, (q, m, name, n, k) in enumerate(prods):
         c = f"linear_{TNAME[q]}_m{m}"
         cls_idx.setdefault(c, []).append(j)
-        cls_bytes[c] = cls_bytes.get(c, 0) + algo_bytes(q, n, k, m)
+        cls_bytes[c] = cls_bytes.get(c, 0) + algo_work(wl, q, n, k, m)
     cls_first = {c: idx[0] for c, idx in cls_idx.items()}
     cls_count = {c: len(idx) for c, idx in cls_idx.items()}
     class_ms: dict[str, float] = {}
@@ -292,17 +322,17 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     dominant = max(class_ms, key=class_ms.get)
     j = cls_first[dominant]
     q, m, _, n, k = prods[j]
-    # One "launch" of the dominant kernel = one product: its decode kernel (plus,
-    # on the tcgen05 path, the small activation split the events also bracket).
+    # One "launch" of the dominant kernel = one product: its linear kernel (plus,
+    # on the fp16 tensor-core paths, the small activation split before it).
     kernels_per_product = _launches_for(lib, linear, calls[j], sh, torch)
     dom_launches = cls_count[dominant]
     dom_bytes_per_launch = cls_bytes[dominant] / dom_launches
     dom_ms_per_launch = class_ms[dominant] / dom_launches
-    peak, peak_kind = peaks()
-    achieved = dom_bytes_per_launch / (dom_ms_per_launch * 1e-3) / 1e9
+    peak, peak_kind = peaks(wl["unit"])
+    achieved = work_rate(wl, dom_bytes_per_launch, dom_ms_per_launch * 1e-3)
     traffic = _traffic(dominant)
 
-    value = bytes_per_step / (ms_per_step * 1e-3) / 1e9  # bytes_per_step is already the whole job's
+    value = work_rate(wl, work_per_step, ms_per_step * 1e-3)  # work_per_step is already the whole job's
 
     # End to end through the public API with host buffers (pinned), same stream.
     e2e_value, e2e_ms = None, None
@@ -334,35 +364,38 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_ms = float(t.item())
-        e2e_value = bytes_per_step / (e2e_ms / args.steps * 1e-3) / 1e9
+        e2e_value = work_rate(wl, work_per_step, e2e_ms / args.steps * 1e-3)
 
     cpu = None
     if keep_host:
-        cpu = cpu_baseline(prods, host_blocks, {key: t.cpu().numpy() for key, t in xs.items()},
+        cpu = cpu_baseline(wl, prods, host_blocks, {key: t.cpu().numpy() for key, t in xs.items()},
                            max_seconds=args.cpu_seconds)
 
     if rank == 0:
         out = {
-            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": METRIC, "value": round(value, 2), "unit": wl["unit"], "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (GGUF Q4_0/Q4_1 weights)",
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (GGUF " + "/".join(TNAME[q].upper() for q in wl["qtypes"]) + " weights)",
             "data": "synthetic (seeded N(0,0.02) weights packed bit-exactly, N(0,1) activations)",
             "config": {"workload": args.workload,
-                       "products": "gate/up 14336x4096, down 4096x14336; Q4_0, Q4_1; M = 1, 4, 16"
-                                   + (f"; rows x{world}, row-sharded" if world > 1 else ""),
-                       "bytes_per_step": bytes_per_step,
-                       "l2": "inputs larger than L2: 627 MB of distinct weights per GPU per step",
+                       "products": wl["desc"] + (f"; rows x{world}, row-sharded" if world > 1 else ""),
+                       ("flops_per_step" if wl["unit"] == "TFLOP/s" else "bytes_per_step"): work_per_step,
+                       "l2": wl["l2"],
                        "parallelism": f"tp{world}: row shards + NCCL all-gather per product" if world > 1
                        else "single GPU"},
-            "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": traffic, "algorithmic_bytes_per_launch": int(dom_bytes_per_launch),
+            "roofline": {"bound": "tensor" if wl["unit"] == "TFLOP/s" else "hbm", "kernel": dominant,
+                         "achieved": round(achieved, 1), "peak": peak,
+                         "unit": wl["unit"], "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": traffic, ("algorithmic_flops_per_launch" if wl["unit"] == "TFLOP/s"
+                                              else "algorithmic_bytes_per_launch"): int(dom_bytes_per_launch),
                          "ms_per_launch": round(dom_ms_per_launch, 6),
-                         "launch": f"one product ({kernels_per_product} kernel(s): decode kernel"
-                                   + (" + activation split)" if kernels_per_product > 1 else ")")},
+                         "launch": f"one product ({kernels_per_product} kernel(s)"
+                                   + (": the linear kernel + its activation split)" if kernels_per_product > 1
+                                      else ")")},
             "per_class_ms": {c: round(v, 5) for c, v in sorted(class_ms.items())},
             "e2e": None if e2e_value is None else {
-                "value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "value": round(e2e_value, 2), "unit": wl["unit"], "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms / args.steps, 6)},
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
@@ -425,7 +458,7 @@ def cpu_threads() -> int:
 
 
 def cpu_run(kind, eng, prods, blocks, xs, threads):
-    """One pass over `prods` on the CPU; returns seconds."""
+    """One pass over `prods` on the CPU (each product over the rows of xs[(m, k)]); returns seconds."""
     if kind == "reference":
         ws = [eng.weight(q, blocks[i], n, k) for i, (q, m, name, n, k) in enumerate(prods)]
         t = time.perf_counter()
@@ -441,18 +474,26 @@ def cpu_run(kind, eng, prods, blocks, xs, threads):
     return time.perf_counter() - t
 
 
-def cpu_baseline(prods, blocks, xs, max_seconds: float = 20.0) -> dict:
+def cpu_baseline(wl, prods, blocks, xs, max_seconds: float = 20.0) -> dict:
     kind, eng = _cpu_engine()
     threads = cpu_threads()
-    bytes_step = sum(algo_bytes(q, n, k, m) for (q, m, _, n, k) in prods)
+    rows = wl["cpu_rows"]
+    if rows:  # a bounded sample: the first `rows` activation rows of every product
+        xs = {key: x[:rows] for key, x in xs.items()}
+        prods = [(q, min(m, rows), name, n, k) for (q, m, name, n, k) in prods]
+        xs = {(min(m, rows), k): x for (m, k), x in xs.items()}
+    work_step = sum(algo_work(wl, q, n, k, m) for (q, m, _, n, k) in prods)
     reps, total = 0, 0.0
     while reps < 1 or (total < max_seconds * 0.5 and reps < 5):
         total += cpu_run(kind, eng, prods, blocks, xs, threads)
         reps += 1
-    return {"value": round(bytes_step * reps / total / 1e9, 4), "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": f"{reps} full step(s) of the workload ({len(prods)} products, {bytes_step} algorithmic bytes"
-                      f" each), LinearDispatch kThreadedSimd per activation row with SetMatmulThreads({threads})"
-                      if kind == "reference" else f"{reps} full step(s), C port of QuantizedDotRow, {threads} threads"}
+    return {"value": round(work_rate(wl, work_step * reps, total), 6), "unit": wl["unit"], "cores": threads,
+            "kind": kind,
+            "sample": (f"{reps} pass(es) over the workload's {len(prods)} products"
+                       + (f" restricted to their first {rows} activation rows" if rows else "")
+                       + f" ({work_step:.4g} units of work each), "
+                       + (f"LinearDispatch kThreadedSimd per activation row with SetMatmulThreads({threads})"
+                          if kind == "reference" else f"C port of QuantizedDotRow, {threads} threads"))}
 
 
 def host_workload(prods, seed: int = 0):
@@ -481,29 +522,33 @@ def run_reference(args, rank: int, world: int) -> None:
         return  # the CPU reference runs once, on rank 0
     wl = WORKLOADS[args.workload]
     prods = products(wl)
+    rows = wl["cpu_rows"]
+    if rows:  # the reference runs prefill row by row: each product is sampled on its first rows
+        prods = [(q, min(m, rows), name, n, k) for (q, m, name, n, k) in prods]
     kind, eng, blocks, xs = host_workload(prods)
     threads = cpu_threads()
     cpu_run(kind, eng, prods[:1], blocks[:1], xs, threads)  # warm the thread pool and caches
     # Each step is a bounded sample of the workload: one of its products, in launch order.
-    bytes_all = [algo_bytes(q, n, k, m) for (q, m, _, n, k) in prods]
-    total_b, total_t = 0, 0.0
+    work_all = [algo_work(wl, q, n, k, m) for (q, m, _, n, k) in prods]
+    total_w, total_t = 0.0, 0.0
     for s in range(args.steps):
         i = s % len(prods)
         total_t += cpu_run(kind, eng, [prods[i]], [blocks[i]], xs, threads)
-        total_b += bytes_all[i]
-    value = total_b / total_t / 1e9
-    sample = (f"each step = one of the workload's {len(prods)} products, in launch order; "
+        total_w += work_all[i]
+    value = work_rate(wl, total_w, total_t)
+    sample = (f"each step = one of the workload's {len(prods)} products, in launch order"
+              + (f", on its first {rows} activation rows" if rows else "") + "; "
               f"{'reference LinearDispatch kThreadedSimd' if kind == 'reference' else 'C port'}, {threads} threads")
-    out = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+    unit = wl["unit"]
+    out = {"metric": METRIC, "value": round(value, 6), "unit": unit, "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": round(total_t / args.steps * 1e3, 3), "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": None, "dtype": "f32 (GGUF Q4_0/Q4_1 weights)",
+           "scaling": "weak", "vs_baseline": None,
+           "dtype": "f32 (GGUF " + "/".join(TNAME[q].upper() for q in wl["qtypes"]) + " weights)",
            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)", "impl": "reference",
-           "config": {"workload": args.workload,
-                      "products": "gate/up 14336x4096, down 4096x14336; Q4_0, Q4_1; M = 1, 4, 16",
-                      "parallelism": f"{threads} host threads"},
-           "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": kind,
+           "config": {"workload": args.workload, "products": wl["desc"], "parallelism": f"{threads} host threads"},
+           "cpu_baseline": {"value": round(value, 6), "unit": unit, "cores": threads, "kind": kind,
                             "sample": sample},
-           "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+           "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
 
