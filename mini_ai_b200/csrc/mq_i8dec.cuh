@@ -49,14 +49,20 @@
 // Persistent stream-K over the tile-major step space, as the other decode
 // kernels: a tile whose K loop is split across CTAs is completed by the last
 // contributor from at most two partial slots per CTA (deterministic order).
-// Warp roles (21 warps): warp 0 bulk copies of the weight chunks; warps 1, 2, 3
+// Warp roles (25 warps): warp 0 bulk copies of the weight chunks; warps 1, 2, 3
 // and 20 MMA issue, one thread each, taking the steps in turn (issuing a
 // tcgen05.mma occupies its thread for about 80 ns, measured on B200, so one
 // issuer could not keep up with HBM); warp 1 also
 // allocates the TMEM; warps 4..7 prep (limb tiles from the L2-resident
 // activations, one step ahead), taking the steps in turn;
-// warps 8..15 unpackers (two per TMEM lane quarter, one quad of 4 blocks
-// each); warps 16..19 drainers (one per lane quarter). Every wait is
+// warps 8..15 unpackers (one or two activation rows: two groups of one warp
+// per TMEM lane quarter taking the steps in turn, a warp converting both quads
+// of its row; three to five rows: all eight on every step, two per lane
+// quarter, one quad of 4 blocks each); warps 16..19 and 21..24 drainers, two
+// groups of one warp per lane quarter taking the steps in turn (an unpack or a
+// drain step is a chain of barrier waits, shared-memory and TMEM accesses
+// and dependent arithmetic: a drain step took about 0.55 us, measured on
+// B200, and one group alone held every product to that step rate). Every wait is
 // bounded in time; a timeout raises the CTA abort flag and the host-visible
 // error flag and every role leaves its loop (drainers keep their loop shape so
 // that their named barriers still match); in-flight bulk copies and MMAs are
@@ -76,9 +82,10 @@
 namespace mq {
 
 constexpr int kI8Rows = 128;
-constexpr int kI8Warps = 21;
+constexpr int kI8Warps = 25;
 constexpr int kI8Issuers = 4;       // MMA issue threads at most (warps 1, 2, 3, 20), taking the steps in turn
 constexpr int kI8Preps = 4;         // prep warps (4..7): step s is built by warp 4 + s % 4
+constexpr int kI8DrainGroups = 2;   // drainer groups (warps 16..19 and 21..24): step s is drained by group s % 2
 constexpr int kI8Threads = kI8Warps * 32;
 constexpr int kI8MaxM = 5;          // activation rows per launch: 3 limbs x 5 rows <= N = 16
 constexpr int kI8N = 16;            // MMA N (B rows)
@@ -122,30 +129,44 @@ struct I8Cfg {
   static constexpr int kRowOff = 16 / G;               // B row offset between the blocks of a pair
   // TMEM: the unpack -> MMA -> completion round trip (~1.1 us measured) gates
   // the A slots, the MMA -> drain round trip (~1 us) the D slots.
-  static constexpr int NA = G == 2 ? 4 : 2;            // A slots in TMEM (64 columns each)
+  static constexpr int NA = 4;                         // A slots in TMEM (64 columns each)
   static constexpr int kACols = 64, kDCols = 8 * kI8N / G, kDOff = NA * kACols;
-  static constexpr int ND = (512 - kDOff) / kDCols;    // D slots in TMEM
+  // D slots in TMEM: a multiple of the drainer groups, so that every phase of
+  // a slot's barrier is released by the same group (in step order).
+  static constexpr int ND = (512 - kDOff) / kDCols / kI8DrainGroups * kI8DrainGroups;
   // Issuers take the steps in turn (each issues a whole step: tcgen05.mma
   // costs its thread ~80 ns, so several steps must be in issue at once). A
   // parity wait is sound only while the awaited phase is the barrier's
   // current or immediately preceding one; with I issuers that holds when every
   // per-step ring (A slots, tiles, commits) is a multiple of I, so that one
-  // issuer owns all phases of a barrier, and ND >= I (the issuer of step s
-  // waited for the drain of s - I - ND before it waits for s - ND).
+  // issuer owns all phases of a barrier, and ND >= I with ND - I a multiple
+  // of the drainer groups (before it waits for the drain of s - ND, the issuer
+  // of step s waited for the drain of s - I - ND, which the group that drains
+  // s - 2 ND drains no earlier).
   static constexpr int I = ND >= 4 ? 4 : (ND >= 2 ? 2 : 1);
-  static_assert(NA % I == 0 && NB % I == 0 && kI8Done % I == 0 && ND >= I, "issuer ownership of the rings");
+  static_assert(NA % I == 0 && NB % I == 0 && kI8Done % I == 0 && ND >= I && (ND - I) % kI8DrainGroups == 0,
+                "issuer ownership of the rings");
   static_assert(kDOff + ND * kDCols <= 512, "TMEM budget");
   static_assert(kI8Preps <= DS && kI8Preps <= kI8Done && DS % kI8Preps == 0, "ring depths (see the waits)");
+  static_assert(DS % kI8DrainGroups == 0 && kI8Done % kI8DrainGroups == 0, "drainer group ownership of the rings");
   static constexpr int kBOff = 0;                               // 1 KB aligned (128-byte swizzle atoms)
   static constexpr int kDrOff = kBOff + NB * kI8BTile;
-  static constexpr int kPkOff = kDrOff + DS * kDrBytes;         // 16-byte aligned bulk destinations
+  static constexpr int kXchOff = kDrOff + DS * kDrBytes;        // drainer groups' tile sums: float[2][128][MC]
+  static constexpr int kPkOff = kXchOff + ((2 * kI8Rows * MC * 4 + 15) / 16) * 16;  // 16-byte aligned bulk destinations
   static constexpr int kPsFit = (222 * 1024 - kPkOff) / kChunk;
-  static constexpr int PS = kPsFit < 12 ? kPsFit : 12;          // weight chunks in flight
+  // Unpacker groups taking the steps in turn (see the unpackers): two for the
+  // paired-block configurations (G == 2), one for the others, the faster
+  // choice for each, measured on B200.
+  static constexpr int UG = G == 2 ? 2 : 1;
+  // Weight chunks in flight: a multiple of UG, so that each chunk slot belongs to one unpacker group.
+  static constexpr int PS = (kPsFit < 12 ? kPsFit : 12) / UG * UG;
   static constexpr int kBarOff = kPkOff + PS * kChunk;
   static constexpr int kNumBars = 2 * PS + NB + 2 * DS + NA + ND + kI8Done + kI8Issuers;
   static constexpr int kBytes = kBarOff + 8 * kNumBars + 16;
   static constexpr int kAlloc = kBytes + 1024;
-  static_assert(PS >= 3 && kAlloc <= 227 * 1024, "shared memory budget");
+  static_assert(PS >= 4 && kAlloc <= 227 * 1024, "shared memory budget");
+  static_assert(PS % UG == 0 && NA % UG == 0 && DS % UG == 0 && kI8Done % UG == 0,
+                "unpacker group ownership of the rings");
   static_assert(kChunk % 16 == 0 && kDrBytes % 16 == 0, "copy alignment");
   // D columns the drainers read per region and regions per batch of TMEM
   // loads (32 registers a batch).
@@ -224,10 +245,10 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
   const int nsteps = g1 - g0;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < PS; ++i) sm100::mbar_init(&pk_full[i], 1), sm100::mbar_init(&pk_empty[i], 8);
+    for (int i = 0; i < PS; ++i) sm100::mbar_init(&pk_full[i], 1), sm100::mbar_init(&pk_empty[i], 8 / L::UG);
     for (int i = 0; i < NB; ++i) sm100::mbar_init(&b_full[i], 1);
     for (int i = 0; i < DS; ++i) sm100::mbar_init(&dr_full[i], 5), sm100::mbar_init(&dr_empty[i], 4);
-    for (int i = 0; i < NA; ++i) sm100::mbar_init(&a_full[i], 8);
+    for (int i = 0; i < NA; ++i) sm100::mbar_init(&a_full[i], 8 / L::UG);
     for (int i = 0; i < ND; ++i) sm100::mbar_init(&d_empty[i], 4);
     for (int i = 0; i < kI8Done; ++i) sm100::mbar_init(&done[i], 1);
     for (int i = 0; i < kI8Issuers; ++i) sm100::mbar_init(&fin[i], 1);
@@ -415,12 +436,19 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
       sm100::mbar_wait(&fin[issuer], 0u, nullptr, nullptr, kI8DrainNs);
     }
   } else if (warp >= 8 && warp < 16) {  // ----------------------- unpackers: packed bytes -> codes in TMEM
-    const int qq = warp & 3;           // TMEM lane quarter
-    const int h = (warp - 8) >> 2;     // quad of the step: A columns 32h..32h+31 of a slot
-    const int r = 32 * qq + lane;      // tile row
+    // UG == 2: two groups of four warps (one per TMEM lane quarter) take the
+    // steps in turn, and a warp converts both quads of its row's step (A
+    // columns 0..31 and 32..63 of the slot). UG == 1: every step by all eight
+    // warps, two per lane quarter, one quad each. The warps of the first quad
+    // (all of them with UG == 2) also move the row's scales into the drain slot.
+    constexpr int UG = L::UG, NQ = UG;  // quads per warp and step
+    const int qq = warp & 3;                // TMEM lane quarter
+    const int hq = UG == 2 ? 0 : (warp - 8) >> 2;
+    const bool scales = hq == 0;
+    const int r = 32 * qq + lane;           // tile row
     const int sw = r & 7;
     const uint32_t lane_base = (uint32_t)(32 * qq) << 16;
-    for (int ls = 0; ls < nsteps; ++ls) {
+    for (int ls = UG == 2 ? (warp - 8) >> 2 : 0; ls < nsteps; ls += UG) {
       const int pi = ls % PS, di = ls % DS;
       // tcgen05.st is warp-collective: every wait result is made warp-uniform.
       bool ok = sm100::mbar_wait_sleep(&pk_full[pi], (uint32_t)(ls / PS) & 1u, a.err, abort, kI8WaitNs);
@@ -428,72 +456,87 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
         const int pd = ls - NA;
         ok = ok && sm100::mbar_wait_sleep(&done[pd % kI8Done], (uint32_t)(pd / kI8Done) & 1u, a.err, abort, kI8WaitNs);
       }
-      if (h == 0 && ls >= DS)  // quad-0 warps also move the step's scales into a drain slot
+      if (scales && ls >= DS)  // the drain slot is free once step ls - DS was drained
         ok = ok && sm100::mbar_wait_sleep(&dr_empty[di], ((uint32_t)(ls / DS) & 1u) ^ 1u, a.err, abort, kI8WaitNs);
       if (!__all_sync(0xffffffffu, ok)) break;
       const uint8_t *chunk = smem + L::kPkOff + pi * L::kChunk;
-      // The quad's packed bytes (and the row's scales) go to registers first;
-      // the chunk is released before they are converted and stored.
-      uint4 sc4 = make_uint4(0u, 0u, 0u, 0u), mn4 = make_uint4(0u, 0u, 0u, 0u);
-      if (h == 0) {
-        sc4 = *reinterpret_cast<const uint4 *>(chunk + L::kPkBytes + r * 16);
-        if constexpr (QT == MQ_Q4_1) mn4 = *reinterpret_cast<const uint4 *>(chunk + L::kPkBytes + kI8Rows * 16 + r * 16);
-      }
-      uint32_t col[32];  // [block j of the quad][8 columns]
-      if constexpr (QT == MQ_Q8_0) {
-        const uint8_t *prow = chunk + h * (kI8Rows * 128) + r * 128;
-        uint32_t cw[8][4];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint4 v = *reinterpret_cast<const uint4 *>(prow + ((c ^ sw) << 4));
-          cw[c][0] = v.x, cw[c][1] = v.y, cw[c][2] = v.z, cw[c][3] = v.w;
-        }
-        __syncwarp();
-        if (lane == 0) sm100::mbar_arrive(&pk_empty[pi]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            col[8 * j + 2 * t] = cw[2 * t + (j >> 1)][2 * (j & 1)];
-            col[8 * j + 2 * t + 1] = cw[2 * t + (j >> 1)][2 * (j & 1) + 1];
-          }
-      } else {
-        const uint8_t *prow = chunk + r * 128;
-        uint4 v4[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) v4[t] = *reinterpret_cast<const uint4 *>(prow + (((4 * h + t) ^ sw) << 4));
-        __syncwarp();
-        if (lane == 0) sm100::mbar_arrive(&pk_empty[pi]);
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const uint32_t wv[4] = {v4[t].x, v4[t].y, v4[t].z, v4[t].w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            col[8 * j + 2 * t] = wv[j] & 0x0F0F0F0Fu;
-            col[8 * j + 2 * t + 1] = (wv[j] >> 4) & 0x0F0F0F0Fu;
-          }
-        }
-      }
-      if (h == 0) {
+      if (scales) {  // the row's scales (and Q4_1 mins) go to the drain slot first
         uint8_t *dr = smem + L::kDrOff + di * L::kDrBytes;
-        *reinterpret_cast<uint4 *>(dr + r * 16) = sc4;
-        if constexpr (QT == MQ_Q4_1) *reinterpret_cast<uint4 *>(dr + kI8Rows * 16 + r * 16) = mn4;
+        *reinterpret_cast<uint4 *>(dr + r * 16) = *reinterpret_cast<const uint4 *>(chunk + L::kPkBytes + r * 16);
+        if constexpr (QT == MQ_Q4_1)
+          *reinterpret_cast<uint4 *>(dr + kI8Rows * 16 + r * 16) =
+              *reinterpret_cast<const uint4 *>(chunk + L::kPkBytes + kI8Rows * 16 + r * 16);
         __syncwarp();
         if (lane == 0) sm100::mbar_arrive(&dr_full[di]);
       }
-      tmem_st_x32(tmem + lane_base + (uint32_t)((ls % NA) * L::kACols + 32 * h), col);
+      const uint32_t acol = tmem + lane_base + (uint32_t)((ls % NA) * L::kACols);
+      uint32_t col[32];  // [block j of the quad][8 columns]
+      if constexpr (QT == MQ_Q8_0) {
+        // 128 code bytes per row and quad: a warp's quads are loaded, converted
+        // and stored one after the other; the chunk is released after the last load.
+#pragma unroll
+        for (int qi = 0; qi < NQ; ++qi) {
+          const int h = hq + qi;
+          const uint8_t *prow = chunk + h * (kI8Rows * 128) + r * 128;
+          uint32_t cw[8][4];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(prow + ((c ^ sw) << 4));
+            cw[c][0] = v.x, cw[c][1] = v.y, cw[c][2] = v.z, cw[c][3] = v.w;
+          }
+          if (qi == NQ - 1) {
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive(&pk_empty[pi]);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              col[8 * j + 2 * t] = cw[2 * t + (j >> 1)][2 * (j & 1)];
+              col[8 * j + 2 * t + 1] = cw[2 * t + (j >> 1)][2 * (j & 1) + 1];
+            }
+          tmem_st_x32(acol + (uint32_t)(32 * h), col);
+        }
+      } else {
+        // 64 packed bytes per row and quad: a warp's quads go to registers and
+        // the chunk is released before they are converted and stored.
+        const uint8_t *prow = chunk + r * 128;
+        uint4 v4[4 * NQ];
+#pragma unroll
+        for (int t = 0; t < 4 * NQ; ++t) v4[t] = *reinterpret_cast<const uint4 *>(prow + (((4 * hq + t) ^ sw) << 4));
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&pk_empty[pi]);
+#pragma unroll
+        for (int qi = 0; qi < NQ; ++qi) {
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const uint4 q = v4[4 * qi + t];
+            const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              col[8 * j + 2 * t] = wv[j] & 0x0F0F0F0Fu;
+              col[8 * j + 2 * t + 1] = (wv[j] >> 4) & 0x0F0F0F0Fu;
+            }
+          }
+          tmem_st_x32(acol + (uint32_t)(32 * (hq + qi)), col);
+        }
+      }
       tmem_st_wait();
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(&a_full[ls % NA]);
     }
-  } else if (warp >= 16 && warp < 20) {  // ------------------------- drainers (TMEM lane = tile row)
-    sm100::griddep_wait();  // outputs, partial slots and tickets may still be in use by the previous kernel
+  } else if (warp >= 16 && warp != 20) {  // ------------------------- drainers (TMEM lane = tile row)
+    // Two groups of four warps (one per TMEM lane quarter) take the steps in
+    // turn: group 1 hands its tile sums to group 0 through shared memory, and
+    // group 0 adds them to its own (fixed order) and completes the tile.
+    const int grp = warp > 20 ? 1 : 0;
+    if (grp == 0) sm100::griddep_wait();  // outputs, partial slots and tickets may still be in use by the previous kernel
     const int qq = warp & 3;
     const int r = 32 * qq + lane;
     const uint32_t lane_base = (uint32_t)(32 * qq) << 16;
     float acc[MC];
-    int cur = -1;
+    float *xch = reinterpret_cast<float *>(smem + L::kXchOff);
     // Completes the tile's output: directly when this CTA owns the whole K loop
     // of the tile, else through the head/tail partial slots and the tile's
     // ticket (the last contributor sums the slots in CTA order).
@@ -547,86 +590,99 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
       // the next tile's slot may reuse this CTA's slot only after s_last is read
       asm volatile("bar.sync 1, 128;" ::: "memory");
     };
-    for (int ls = 0; ls < nsteps; ++ls) {
-      const int g = g0 + ls, tile = g / S;
-      if (tile != cur) {
-        if (cur >= 0) flush(cur);
-        cur = tile;
+    // Every tile that the CTA's step range touches, in order; both groups visit
+    // each one (a group may own no step of a short tile piece) and meet on
+    // named barrier 2 at its end. The exchange buffer alternates between two
+    // halves, so a group-1 write for the next tile cannot meet a group-0 read.
+    const int tfirst = g0 / S, tlast = nsteps > 0 ? (g1 - 1) / S : tfirst - 1;
+    for (int tile = tfirst; tile <= tlast; ++tile) {
+      const int lo = max(g0, tile * S) - g0, hi = min(g1, (tile + 1) * S) - g0;
 #pragma unroll
-        for (int c = 0; c < MC; ++c) acc[c] = 0.0f;
-      }
-      const int di = ls % DS;
-      // Failed waits do not leave the loop: every drainer must run the same
-      // sequence of flushes (they synchronise on a named barrier).
-      bool ok = sm100::mbar_wait_sleep(&dr_full[di], (uint32_t)(ls / DS) & 1u, a.err, abort, kI8WaitNs);
-      ok = ok && sm100::mbar_wait_sleep(&done[ls % kI8Done], (uint32_t)(ls / kI8Done) & 1u, a.err, abort, kI8WaitNs);
-      ok = __all_sync(0xffffffffu, ok);
-      sm100::tc_fence_after();
-      const uint8_t *dr = smem + L::kDrOff + di * L::kDrBytes;
-      const uint4 dq = *reinterpret_cast<const uint4 *>(dr + r * 16);
-      uint4 mq4 = make_uint4(0u, 0u, 0u, 0u);
-      if constexpr (QT == MQ_Q4_1) mq4 = *reinterpret_cast<const uint4 *>(dr + kI8Rows * 16 + r * 16);
-      const uint32_t dw[4] = {dq.x, dq.y, dq.z, dq.w};
-      const uint32_t mw[4] = {mq4.x, mq4.y, mq4.z, mq4.w};
-      const float *inv = reinterpret_cast<const float *>(dr + L::kDrHdr + kI8HdrInv);
-      const int *sx = reinterpret_cast<const int *>(dr + L::kDrHdr + kI8HdrSx);
-      const uint32_t dbase = tmem + lane_base + (uint32_t)(L::kDOff + (ls % ND) * L::kDCols);
-      float st[MC];  // this step's sum, in the step's activation scale
+      for (int c = 0; c < MC; ++c) acc[c] = 0.0f;
+      for (int ls = lo + ((lo & 1) != grp); ls < hi; ls += kI8DrainGroups) {
+        const int di = ls % DS;
+        // Failed waits do not leave the loop: every drainer must run the same
+        // sequence of flushes (they synchronise on a named barrier).
+        bool ok = sm100::mbar_wait_sleep(&dr_full[di], (uint32_t)(ls / DS) & 1u, a.err, abort, kI8WaitNs);
+        ok = ok && sm100::mbar_wait_sleep(&done[ls % kI8Done], (uint32_t)(ls / kI8Done) & 1u, a.err, abort, kI8WaitNs);
+        ok = __all_sync(0xffffffffu, ok);
+        sm100::tc_fence_after();
+        const uint8_t *dr = smem + L::kDrOff + di * L::kDrBytes;
+        const uint4 dq = *reinterpret_cast<const uint4 *>(dr + r * 16);
+        uint4 mq4 = make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (QT == MQ_Q4_1) mq4 = *reinterpret_cast<const uint4 *>(dr + kI8Rows * 16 + r * 16);
+        const uint32_t dw[4] = {dq.x, dq.y, dq.z, dq.w};
+        const uint32_t mw[4] = {mq4.x, mq4.y, mq4.z, mq4.w};
+        const float *inv = reinterpret_cast<const float *>(dr + L::kDrHdr + kI8HdrInv);
+        const int *sx = reinterpret_cast<const int *>(dr + L::kDrHdr + kI8HdrSx);
+        const uint32_t dbase = tmem + lane_base + (uint32_t)(L::kDOff + (ls % ND) * L::kDCols);
+        float st[MC];  // this step's sum, in the step's activation scale
 #pragma unroll
-      for (int c = 0; c < MC; ++c) st[c] = 0.0f;
-      constexpr int kRegions = 8 / L::G;
+        for (int c = 0; c < MC; ++c) st[c] = 0.0f;
+        constexpr int kRegions = 8 / L::G;
 #pragma unroll
-      for (int r0 = 0; r0 < kRegions; r0 += BB) {
-        uint32_t v[BB * NCOL];
-        if (ok) {
+        for (int r0 = 0; r0 < kRegions; r0 += BB) {
+          uint32_t v[BB * NCOL];
+          if (ok) {
 #pragma unroll
-          for (int rb = 0; rb < BB; ++rb) tmem_ld_cols<NCOL>(dbase + (uint32_t)((r0 + rb) * kI8N), &v[rb * NCOL]);
-          sm100::tmem_ld_wait();
-        } else {
+            for (int rb = 0; rb < BB; ++rb) tmem_ld_cols<NCOL>(dbase + (uint32_t)((r0 + rb) * kI8N), &v[rb * NCOL]);
+            sm100::tmem_ld_wait();
+          } else {
 #pragma unroll
-          for (int c = 0; c < BB * NCOL; ++c) v[c] = 0u;
-        }
-        if (r0 + BB == kRegions) {  // the D slot is released before the last batch's arithmetic
-          sm100::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) sm100::mbar_arrive(&d_empty[ls % ND]);
-        }
-#pragma unroll
-        for (int jb = 0; jb < BB * L::G; ++jb) {
-          const int j = r0 * L::G + jb;
-          const __half2 d2 = *reinterpret_cast<const __half2 *>(&dw[j >> 1]);
-          const float d = (j & 1) ? __high2float(d2) : __low2float(d2);
-          float mn = 0.0f;
-          if constexpr (QT == MQ_Q4_1) {
-            const __half2 m2 = *reinterpret_cast<const __half2 *>(&mw[j >> 1]);
-            mn = (j & 1) ? __high2float(m2) : __low2float(m2);
+            for (int c = 0; c < BB * NCOL; ++c) v[c] = 0u;
           }
-          const uint32_t *vb = &v[(jb / L::G) * NCOL + (jb % L::G) * L::kRowOff];
+          if (r0 + BB == kRegions) {  // the D slot is released before the last batch's arithmetic
+            sm100::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive(&d_empty[ls % ND]);
+          }
 #pragma unroll
-          for (int c = 0; c < MC; ++c) {
-            const int l0 = (int)vb[3 * c], l1 = (int)vb[3 * c + 1], l2 = (int)vb[3 * c + 2];
-            if constexpr (QT == MQ_Q8_0) {
-              const int v01 = l0 + (int)((uint32_t)l1 << 8);  // |.| < 2^27: exact
-              st[c] = fmaf(d, fmaf((float)l2, 65536.0f, (float)v01), st[c]);
-            } else {
-              // sum q * X fits int32, so the wrapping combination is exact.
-              int vv = (int)((uint32_t)l0 + ((uint32_t)l1 << 8) + ((uint32_t)l2 << 16));
-              if constexpr (QT == MQ_Q4_0) {
-                vv = (int)((uint32_t)vv - ((uint32_t)sx[j * 8 + c] << 3));
-                st[c] = fmaf(d, (float)vv, st[c]);
+          for (int jb = 0; jb < BB * L::G; ++jb) {
+            const int j = r0 * L::G + jb;
+            const __half2 d2 = *reinterpret_cast<const __half2 *>(&dw[j >> 1]);
+            const float d = (j & 1) ? __high2float(d2) : __low2float(d2);
+            float mn = 0.0f;
+            if constexpr (QT == MQ_Q4_1) {
+              const __half2 m2 = *reinterpret_cast<const __half2 *>(&mw[j >> 1]);
+              mn = (j & 1) ? __high2float(m2) : __low2float(m2);
+            }
+            const uint32_t *vb = &v[(jb / L::G) * NCOL + (jb % L::G) * L::kRowOff];
+#pragma unroll
+            for (int c = 0; c < MC; ++c) {
+              const int l0 = (int)vb[3 * c], l1 = (int)vb[3 * c + 1], l2 = (int)vb[3 * c + 2];
+              if constexpr (QT == MQ_Q8_0) {
+                const int v01 = l0 + (int)((uint32_t)l1 << 8);  // |.| < 2^27: exact
+                st[c] = fmaf(d, fmaf((float)l2, 65536.0f, (float)v01), st[c]);
               } else {
-                st[c] = fmaf(d, (float)vv, fmaf(mn, (float)sx[j * 8 + c], st[c]));
+                // sum q * X fits int32, so the wrapping combination is exact.
+                int vv = (int)((uint32_t)l0 + ((uint32_t)l1 << 8) + ((uint32_t)l2 << 16));
+                if constexpr (QT == MQ_Q4_0) {
+                  vv = (int)((uint32_t)vv - ((uint32_t)sx[j * 8 + c] << 3));
+                  st[c] = fmaf(d, (float)vv, st[c]);
+                } else {
+                  st[c] = fmaf(d, (float)vv, fmaf(mn, (float)sx[j * 8 + c], st[c]));
+                }
               }
             }
           }
         }
-      }
 #pragma unroll
-      for (int c = 0; c < MC; ++c) acc[c] = fmaf(st[c], inv[c], acc[c]);
-      __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(&dr_empty[di]);
+        for (int c = 0; c < MC; ++c) acc[c] = fmaf(st[c], inv[c], acc[c]);
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&dr_empty[di]);
+      }
+      float *xb = xch + ((int64_t)((tile - tfirst) & 1) * kI8Rows + r) * MC;
+      if (grp == 1) {
+#pragma unroll
+        for (int c = 0; c < MC; ++c) xb[c] = acc[c];
+      }
+      asm volatile("bar.sync 2, 256;" ::: "memory");
+      if (grp == 0) {
+#pragma unroll
+        for (int c = 0; c < MC; ++c) acc[c] += xb[c];
+        flush(tile);
+      }
     }
-    if (cur >= 0) flush(cur);
   }
 
   sm100::tc_fence_before();
