@@ -178,7 +178,7 @@ cudaError_t launch_tcdec_t(const CUtensorMap &tx, const DecArgs &a, int grid, cu
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  const cudaError_t e = launch_pdl(tcdec_kernel<QT, BN, NC>, dim3(grid), dim3(kDecThreads), L::kAlloc, s, tx, a);
+  const cudaError_t e = launch_pdl(tcdec_kernel<QT, BN, NC>, dim3(grid), dim3(L::kThreads), L::kAlloc, s, tx, a);
   count_launch();
   return e;
 }

@@ -42,9 +42,9 @@
 // restarts; a tile whose K loop is split across CTAs is completed by the last
 // contributor from at most two partial slots per CTA (deterministic order).
 // A packed step is 8 quant blocks (256 K) = two quads of 4 blocks.
-// Warp roles (16 warps; every role that blocks on an mbarrier has a warp of
-// its own, since a lane suspended in try_wait holds up the diverged lanes of
-// its warp):
+// Warp roles (20 warps, 16 for 32 activation rows; every role that blocks on
+// an mbarrier has a warp of its own, since a lane suspended in try_wait holds
+// up the diverged lanes of its warp):
 //   warp 0         bulk copies of each step's weight chunk: packed quant rows
 //                  (pre-swizzled, PS stages) and fp16 block scales (+ Q4_1
 //                  mins, SS stages);
@@ -54,9 +54,13 @@
 //   warps 4..11    decoders: two per TMEM lane quarter, one per K half of
 //                  every block; packed bytes -> exact fp16 codes -> one
 //                  tcgen05.st per quad into the A ring (one quad a slot);
-//   warps 12..15   drainers: per group, TMEM -> registers, scale in fp32;
-//                  flush per tile (x row scale 2^-e, bias, store or partial +
-//                  ticket).
+//   warps 12..19   drainers, two sets of one warp per lane quarter taking
+//                  the D groups in turn (one set for 32 rows): per group,
+//                  TMEM -> registers, scale in fp32; flush per tile (x row
+//                  scale 2^-e, bias, store or partial + ticket) by set 0 after
+//                  adding set 1's sums. A group's drain is a chain of barrier
+//                  wait, TMEM loads and dependent arithmetic that one set
+//                  alone ran at well under the MMA rate (measured on B200).
 // Launched with programmatic stream serialization after the activation split:
 // TMEM allocation and the weight stream start while the split still runs; the
 // activation TMA and the drainers wait for it (griddepcontrol.wait).
@@ -77,8 +81,7 @@
 namespace mq {
 
 constexpr int kDecRows = 128;
-constexpr int kDecWarps = 16;
-constexpr int kDecThreads = kDecWarps * 32;
+constexpr int kDecWarps = 16;  // without the second drainer set
 constexpr int kDecBlocksPerStep = 8;  // quant blocks per packed step (Q4_x: 128 B per row, Q8_0: 256 B)
 constexpr int kDecGroupBars = 16;     // commit barriers, one per group in a ring
 constexpr uint64_t kDecWaitNs = 1000000000ull;
@@ -129,8 +132,17 @@ struct DecCfg {
   // Two issuers take alternate quads. With G = 1 a quad's four groups use
   // every D slot, so both issuers would wait on the same slots: one issuer.
   static constexpr int kIssuers = G == 1 ? 1 : 2;
+  // Drainer sets (warps 12..15, and 16..19 when there are two): set s drains
+  // the D groups gi with gi % DSETS == s, so each D slot (ND is a multiple of
+  // DSETS) and each commit barrier is released / awaited by one set in order.
+  // The 32-row configuration keeps one set: its drain needs the registers.
+  static constexpr int DSETS = N == 64 ? 1 : 2;
+  static constexpr int kThreads = (kDecWarps + 4 * (DSETS - 1)) * 32;
+  static_assert(ND % DSETS == 0 && kDecGroupBars % DSETS == 0 && (kDecBlocksPerStep / G) % DSETS == 0,
+                "drainer set ownership of the D slots and commit barriers");
   static constexpr int kNumBars = 2 * PS + 2 * SS + XS + NA + ND + kDecGroupBars + 2;
-  static constexpr int kBytes = kBarOff + 8 * kNumBars + 16;
+  static constexpr int kXchOff = (kBarOff + 8 * kNumBars + 16 + 15) / 16 * 16;  // set 1's tile sums: float[2][128][BN]
+  static constexpr int kBytes = kXchOff + (DSETS > 1 ? 2 * kDecRows * BN * 4 : 0);
   // At least 116 KB, so that a second CTA (and its 512-column TMEM request)
   // never lands on an SM this kernel already occupies.
   static constexpr int kAlloc = (kBytes + 1024) > 118784 ? (kBytes + 1024) : 118784;
@@ -216,7 +228,7 @@ __device__ __forceinline__ void tmem_ld_n(uint32_t taddr, uint32_t (&r)[N]) {
 }
 
 template <int QT, int BN, int NC>
-__global__ void __launch_bounds__(kDecThreads, 1)
+__global__ void __launch_bounds__(DecCfg<QT, BN>::kThreads, 1)
     tcdec_kernel(const __grid_constant__ CUtensorMap tm_x, const DecArgs a) {
   using L = DecCfg<QT, BN>;
   constexpr int PS = L::PS, SS = L::SS, XS = L::XS, NA = L::NA, ND = L::ND, G = L::G, N = L::N;
@@ -243,7 +255,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < PS; ++i) sm100::mbar_init(&pk_full[i], 1), sm100::mbar_init(&pk_empty[i], 8);
-    for (int i = 0; i < SS; ++i) sm100::mbar_init(&sc_full[i], 1), sm100::mbar_init(&sc_empty[i], 4);
+    for (int i = 0; i < SS; ++i) sm100::mbar_init(&sc_full[i], 1), sm100::mbar_init(&sc_empty[i], 4 * L::DSETS);
     for (int i = 0; i < XS; ++i) sm100::mbar_init(&x_full[i], 1);
     for (int i = 0; i < NA; ++i) sm100::mbar_init(&a_full[i], 8);
     for (int i = 0; i < ND; ++i) sm100::mbar_init(&d_empty[i], 4);
@@ -435,12 +447,17 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       if (lane == 0) sm100::mbar_arrive(&pk_empty[pi]);
     }
   } else {  // ------------------------------------------------ drainers (TMEM lane = tile row)
+    // DSETS sets of four warps (one per TMEM lane quarter); set ds drains the
+    // D groups gi = ds, ds + DSETS, ... of every step. Set 1 hands its tile
+    // sums to set 0 through shared memory, and set 0 adds them to its own
+    // (fixed order) and completes the tile.
+    constexpr int DSETS = L::DSETS;
+    const int ds = (warp - 12) >> 2;
     sm100::griddep_wait();  // block sums, row scales, outputs and workspace
     const int qq = warp & 3;
     const int r = 32 * qq + lane;
     const uint32_t lane_base = (uint32_t)(32 * qq) << 16;
     float acc[NC];
-    int cur = -1;
     // Completes the tile's output: directly when this CTA owns the whole K loop
     // of the tile, else through the head/tail partial slots and the tile's
     // ticket (the last contributor sums the slots in CTA order).
@@ -498,136 +515,150 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       // the next tile's slot may reuse this CTA's slot only after s_last is read
       asm volatile("bar.sync 1, 128;" ::: "memory");
     };
-    for (int ls = 0; ls < nsteps; ++ls) {
-      const int g = g0 + ls, tile = g / S, kstep = g % S;
-      if (tile != cur) {
-        if (cur >= 0) flush(cur);
-        cur = tile;
+    // Every tile that the CTA's step range touches, in order; the sets meet on
+    // named barrier 2 at its end (the exchange buffer alternates between two
+    // halves, so a set-1 write for the next tile cannot meet a set-0 read).
+    const int tfirst = g0 / S, tlast = nsteps > 0 ? (g1 - 1) / S : tfirst - 1;
+    for (int tile = tfirst; tile <= tlast; ++tile) {
+      const int lo = max(g0, tile * S) - g0, hi = min(g1, (tile + 1) * S) - g0;
 #pragma unroll
-        for (int c = 0; c < NC; ++c) acc[c] = 0.0f;
-      }
-      const int si = ls % SS;
-      // Failed waits do not leave the loop: every drainer must run the same
-      // sequence of flushes (they synchronise on a named barrier).
-      const bool sc_ok = sm100::mbar_wait_sleep(&sc_full[si], (uint32_t)(ls / SS) & 1u, a.err, abort, kDecWaitNs);
-      const uint8_t *sc = smem + L::kScOff + si * L::kScBytes;
-      const uint4 dq = *reinterpret_cast<const uint4 *>(sc + r * 16);
-      uint4 mq = make_uint4(0u, 0u, 0u, 0u);
-      if constexpr (QT == MQ_Q4_1) mq = *reinterpret_cast<const uint4 *>(sc + kDecRows * 16 + r * 16);
-      const uint32_t dw[4] = {dq.x, dq.y, dq.z, dq.w};
-      const uint32_t mw[4] = {mq.x, mq.y, mq.z, mq.w};
-      float st[NC];  // this step's sum, in the step's activation scale
+      for (int c = 0; c < NC; ++c) acc[c] = 0.0f;
+      for (int ls = lo; ls < hi; ++ls) {
+        const int kstep = (g0 + ls) % S;
+        const int si = ls % SS;
+        // Failed waits do not leave the loop: every drainer must run the same
+        // sequence of flushes (they synchronise on a named barrier).
+        const bool sc_ok = sm100::mbar_wait_sleep(&sc_full[si], (uint32_t)(ls / SS) & 1u, a.err, abort, kDecWaitNs);
+        const uint8_t *sc = smem + L::kScOff + si * L::kScBytes;
+        const uint4 dq = *reinterpret_cast<const uint4 *>(sc + r * 16);
+        uint4 mq = make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (QT == MQ_Q4_1) mq = *reinterpret_cast<const uint4 *>(sc + kDecRows * 16 + r * 16);
+        const uint32_t dw[4] = {dq.x, dq.y, dq.z, dq.w};
+        const uint32_t mw[4] = {mq.x, mq.y, mq.z, mq.w};
+        float st[NC];  // this step's sum, in the step's activation scale
 #pragma unroll
-      for (int c = 0; c < NC; ++c) st[c] = 0.0f;
+        for (int c = 0; c < NC; ++c) st[c] = 0.0f;
 #pragma unroll
-      for (int gl = 0; gl < kGroupsPerStep; ++gl) {
-        const int gi = ls * kGroupsPerStep + gl;
-        bool ok = sm100::mbar_wait_sleep(&grp_done[gi % NGB], (uint32_t)(gi / NGB) & 1u, a.err, abort, kDecWaitNs);
-        ok = __all_sync(0xffffffffu, ok && sc_ok);
-        sm100::tc_fence_after();
-        const uint32_t dbase = tmem + lane_base + (uint32_t)(L::kDOff + (gi % ND) * L::kDCols);
-        if constexpr (N == 64) {
-          // 32 activation rows (G = 1): the hi and lo halves one after the other,
-          // so that a half, the step sum and the accumulator fit the registers.
-          const int jb = gl;
-          const __half2 d2 = *reinterpret_cast<const __half2 *>(&dw[jb >> 1]);
-          const float d = (jb & 1) ? __high2float(d2) : __low2float(d2);
+        for (int gl = ds; gl < kGroupsPerStep; gl += DSETS) {
+          const int gi = ls * kGroupsPerStep + gl;
+          bool ok = sm100::mbar_wait_sleep(&grp_done[gi % NGB], (uint32_t)(gi / NGB) & 1u, a.err, abort, kDecWaitNs);
+          ok = __all_sync(0xffffffffu, ok && sc_ok);
+          sm100::tc_fence_after();
+          const uint32_t dbase = tmem + lane_base + (uint32_t)(L::kDOff + (gi % ND) * L::kDCols);
+          if constexpr (N == 64) {
+            // 32 activation rows (G = 1): the hi and lo halves one after the other,
+            // so that a half, the step sum and the accumulator fit the registers.
+            const int jb = gl;
+            const __half2 d2 = *reinterpret_cast<const __half2 *>(&dw[jb >> 1]);
+            const float d = (jb & 1) ? __high2float(d2) : __low2float(d2);
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t vh[32];
+            for (int half = 0; half < 2; ++half) {
+              uint32_t vh[32];
+              if (ok) {
+                sm100::tmem_ld_32x32b_x32(dbase + (uint32_t)(32 * half), vh);
+                sm100::tmem_ld_wait();
+              } else {
+#pragma unroll
+                for (int c = 0; c < 32; ++c) vh[c] = 0u;
+              }
+#pragma unroll
+              for (int c = 0; c < NC; c += 2) {
+                const float2 r2 = __ffma2_rn(make_float2(d, d), make_float2(__uint_as_float(vh[c]), __uint_as_float(vh[c + 1])),
+                                             make_float2(st[c], st[c + 1]));
+                st[c] = r2.x, st[c + 1] = r2.y;
+              }
+            }
+            sm100::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive(&d_empty[gi % ND]);
+            if constexpr (QT == MQ_Q4_1) {
+              const __half2 m2 = *reinterpret_cast<const __half2 *>(&mw[jb >> 1]);
+              const float mm = (jb & 1) ? __high2float(m2) : __low2float(m2);
+              const float4 *xs =
+                  reinterpret_cast<const float4 *>(a.xsum + (int64_t)(kstep * kDecBlocksPerStep + jb) * BN);
+#pragma unroll
+              for (int c = 0; c < NC; c += 4) {
+                const float4 s4 = __ldg(xs + c / 4);
+                st[c] = fmaf(mm, s4.x, st[c]);
+                st[c + 1] = fmaf(mm, s4.y, st[c + 1]);
+                st[c + 2] = fmaf(mm, s4.z, st[c + 2]);
+                st[c + 3] = fmaf(mm, s4.w, st[c + 3]);
+              }
+            }
+            continue;
+          }
+          // One block at a time (N columns: the hi rows, then the lo rows); the
+          // D slot is released once the group's last block is in registers.
+#pragma unroll
+          for (int jg = 0; jg < G; ++jg) {
+            const int jb = gl * G + jg;  // block of the step
+            uint32_t vb[N];
             if (ok) {
-              sm100::tmem_ld_32x32b_x32(dbase + (uint32_t)(32 * half), vh);
+              tmem_ld_n<N>(dbase + (uint32_t)(jg * N), vb);
               sm100::tmem_ld_wait();
             } else {
 #pragma unroll
-              for (int c = 0; c < 32; ++c) vh[c] = 0u;
+              for (int c = 0; c < N; ++c) vb[c] = 0u;
             }
+            if (jg == G - 1) {
+              sm100::tc_fence_before();
+              __syncwarp();
+              if (lane == 0) sm100::mbar_arrive(&d_empty[gi % ND]);
+            }
+            const __half2 d2 = *reinterpret_cast<const __half2 *>(&dw[jb >> 1]);
+            const float d = (jb & 1) ? __high2float(d2) : __low2float(d2);
 #pragma unroll
             for (int c = 0; c < NC; c += 2) {
-              const float2 r2 = __ffma2_rn(make_float2(d, d), make_float2(__uint_as_float(vh[c]), __uint_as_float(vh[c + 1])),
-                                           make_float2(st[c], st[c + 1]));
+              float2 r2 = __ffma2_rn(make_float2(d, d), make_float2(__uint_as_float(vb[c]), __uint_as_float(vb[c + 1])),
+                                     make_float2(st[c], st[c + 1]));
+              r2 = __ffma2_rn(make_float2(d, d),
+                              make_float2(__uint_as_float(vb[BN + c]), __uint_as_float(vb[BN + c + 1])), r2);
               st[c] = r2.x, st[c + 1] = r2.y;
             }
-          }
-          sm100::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) sm100::mbar_arrive(&d_empty[gi % ND]);
-          if constexpr (QT == MQ_Q4_1) {
-            const __half2 m2 = *reinterpret_cast<const __half2 *>(&mw[jb >> 1]);
-            const float mm = (jb & 1) ? __high2float(m2) : __low2float(m2);
-            const float4 *xs =
-                reinterpret_cast<const float4 *>(a.xsum + (int64_t)(kstep * kDecBlocksPerStep + jb) * BN);
+            if constexpr (QT == MQ_Q4_1) {
+              const __half2 m2 = *reinterpret_cast<const __half2 *>(&mw[jb >> 1]);
+              const float mm = (jb & 1) ? __high2float(m2) : __low2float(m2);
+              const float4 *xs =
+                  reinterpret_cast<const float4 *>(a.xsum + (int64_t)(kstep * kDecBlocksPerStep + jb) * BN);
 #pragma unroll
-            for (int c = 0; c < NC; c += 4) {
-              const float4 s4 = __ldg(xs + c / 4);
-              st[c] = fmaf(mm, s4.x, st[c]);
-              st[c + 1] = fmaf(mm, s4.y, st[c + 1]);
-              st[c + 2] = fmaf(mm, s4.z, st[c + 2]);
-              st[c + 3] = fmaf(mm, s4.w, st[c + 3]);
+              for (int c = 0; c < NC; c += 4) {
+                const float4 s4 = __ldg(xs + c / 4);
+                st[c] = fmaf(mm, s4.x, st[c]);
+                st[c + 1] = fmaf(mm, s4.y, st[c + 1]);
+                st[c + 2] = fmaf(mm, s4.z, st[c + 2]);
+                st[c + 3] = fmaf(mm, s4.w, st[c + 3]);
+              }
             }
           }
-          continue;
         }
-        // The whole group in one batch of loads and one wait; the D slot is
-        // released before the arithmetic.
-        uint32_t v[G * N];
-        if (ok) {
+        {  // back to x's own scale: 2^-e of this step
+          const float4 *inv = reinterpret_cast<const float4 *>(a.xinv + (int64_t)kstep * BN);
 #pragma unroll
-          for (int jg = 0; jg < G; ++jg)
-            tmem_ld_n<N>(dbase + (uint32_t)(jg * N), *reinterpret_cast<uint32_t(*)[N]>(&v[jg * N]));
-          sm100::tmem_ld_wait();
-        } else {
-#pragma unroll
-          for (int c = 0; c < G * N; ++c) v[c] = 0u;
+          for (int c = 0; c < NC; c += 4) {
+            const float4 v4 = __ldg(inv + c / 4);
+            acc[c] = fmaf(st[c], v4.x, acc[c]);
+            acc[c + 1] = fmaf(st[c + 1], v4.y, acc[c + 1]);
+            acc[c + 2] = fmaf(st[c + 2], v4.z, acc[c + 2]);
+            acc[c + 3] = fmaf(st[c + 3], v4.w, acc[c + 3]);
+          }
         }
-        sm100::tc_fence_before();
         __syncwarp();
-        if (lane == 0) sm100::mbar_arrive(&d_empty[gi % ND]);
+        if (lane == 0) sm100::mbar_arrive(&sc_empty[si]);
+      }
+      if constexpr (DSETS > 1) {
+        float *xb = reinterpret_cast<float *>(smem + L::kXchOff) + ((int64_t)((tile - tfirst) & 1) * kDecRows + r) * BN;
+        if (ds == 1) {
 #pragma unroll
-        for (int jg = 0; jg < G; ++jg) {
-          const int jb = gl * G + jg;  // block of the step
-          const uint32_t *vb = &v[jg * N];
-          const __half2 d2 = *reinterpret_cast<const __half2 *>(&dw[jb >> 1]);
-          const float d = (jb & 1) ? __high2float(d2) : __low2float(d2);
+          for (int c = 0; c < NC; ++c) xb[c] = acc[c];
+        }
+        asm volatile("bar.sync 2, 256;" ::: "memory");
+        if (ds == 0) {
 #pragma unroll
-          for (int c = 0; c < NC; c += 2) {
-            float2 r2 = __ffma2_rn(make_float2(d, d), make_float2(__uint_as_float(vb[c]), __uint_as_float(vb[c + 1])),
-                                   make_float2(st[c], st[c + 1]));
-            r2 = __ffma2_rn(make_float2(d, d),
-                            make_float2(__uint_as_float(vb[BN + c]), __uint_as_float(vb[BN + c + 1])), r2);
-            st[c] = r2.x, st[c + 1] = r2.y;
-          }
-          if constexpr (QT == MQ_Q4_1) {
-            const __half2 m2 = *reinterpret_cast<const __half2 *>(&mw[jb >> 1]);
-            const float mm = (jb & 1) ? __high2float(m2) : __low2float(m2);
-            const float4 *xs =
-                reinterpret_cast<const float4 *>(a.xsum + (int64_t)(kstep * kDecBlocksPerStep + jb) * BN);
-#pragma unroll
-            for (int c = 0; c < NC; c += 4) {
-              const float4 s4 = __ldg(xs + c / 4);
-              st[c] = fmaf(mm, s4.x, st[c]);
-              st[c + 1] = fmaf(mm, s4.y, st[c + 1]);
-              st[c + 2] = fmaf(mm, s4.z, st[c + 2]);
-              st[c + 3] = fmaf(mm, s4.w, st[c + 3]);
-            }
-          }
+          for (int c = 0; c < NC; ++c) acc[c] += xb[c];
         }
       }
-      {  // back to x's own scale: 2^-e of this step
-        const float4 *inv = reinterpret_cast<const float4 *>(a.xinv + (int64_t)kstep * BN);
-#pragma unroll
-        for (int c = 0; c < NC; c += 4) {
-          const float4 v4 = __ldg(inv + c / 4);
-          acc[c] = fmaf(st[c], v4.x, acc[c]);
-          acc[c + 1] = fmaf(st[c + 1], v4.y, acc[c + 1]);
-          acc[c + 2] = fmaf(st[c + 2], v4.z, acc[c + 2]);
-          acc[c + 3] = fmaf(st[c + 3], v4.w, acc[c + 3]);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(&sc_empty[si]);
+      if (ds == 0) flush(tile);
     }
-    if (cur >= 0) flush(cur);
   }
 
   sm100::tc_fence_before();
