@@ -160,7 +160,13 @@ typedef struct mq_comm mq_comm;
 int mq_comm_unique_id(void *id, size_t len);
 
 /* Join the communicator of `nranks` ranks as `rank`, on `device`. Collective:
- * every rank must call it with the same id. */
+ * every rank must call it with the same id. With MQ_P2P_GATHER=1 in every
+ * rank's environment (and 2..8 ranks) it also allocates a staging region of
+ * 2 * nranks * 4 MiB on `device` and maps every peer's region through CUDA
+ * IPC, so that mq_linear_sharded_allgather gathers over NVLink peer memory
+ * instead of NCCL; if any rank cannot map every peer, all ranks use NCCL.
+ * Destroy the communicators only after every rank's last gather completed
+ * (for example after a barrier). */
 int mq_comm_create(int device, int nranks, int rank, const void *id, size_t len, mq_comm **out);
 void mq_comm_destroy(mq_comm *c);
 
@@ -168,7 +174,10 @@ void mq_comm_destroy(mq_comm *c);
  * (+ bias[rank*R .. rank*R+R) when bias, the full [N] vector, is given) and
  * an all-gather of the slices. x: device F32 [m, ldx] (full K); y: device F32
  * [m, ldy] with ldy >= N. Stream-ordered on `stream`; every rank must call it
- * with the same m, in the same order relative to its other collectives. */
+ * with the same m, in the same order relative to its other collectives. The
+ * peer-memory gather (see mq_comm_create) takes outputs with m * R <= 2^20 and
+ * may be captured in a CUDA graph; a peer that does not arrive within 1 s
+ * makes the next call on this device fail with MQ_ERR_TIMEOUT. */
 int mq_linear_sharded_allgather(const mq_weight *shard, const float *x, int m, int ldx, const float *bias,
                                 float *y, int ldy, mq_comm *comm, void *stream);
 

@@ -1,4 +1,4 @@
-// Row-sharded linear with an NCCL all-gather of the output slices.
+// Row-sharded linear with an all-gather of the output slices over NVLink.
 //
 // A projection too large for one GPU (or worth splitting for bandwidth) is
 // split by output rows: rank r of G holds rows [r*R, (r+1)*R) as its own
@@ -7,6 +7,23 @@
 // kernels and one all-gather over NVLink assembles y [m, G*R] on every rank.
 // The result is bit-identical to the unsharded product: the same kernels see
 // the same rows.
+//
+// The gather runs over peer memory: at communicator creation every rank
+// allocates a staging region ([2 halves][nranks slots][kP2PSlotFloats] floats,
+// then [2][nranks] arrival flags and three local counters), and the ranks
+// exchange CUDA IPC handles for it (through NCCL) and map each other's
+// regions. Per call, after the rank's decode kernel has written its slice into
+// its own output, a push kernel stores the slice into every peer's slot of the
+// current half and, once all its CTAs' stores are fenced at system scope,
+// raises this rank's flag in every peer's region (release store); a pull
+// kernel waits (bounded, 1 s) for every peer's flag (acquire load) and copies
+// the peers' slices from the local staging into the output. The epoch (and
+// with it the half) lives in device memory and is advanced by the pull
+// kernel, so a CUDA graph that captured these launches replays correctly.
+// A rank can be at most one call ahead of a peer (its next push waits for the
+// peer's flags of the current call), so two halves are enough. Outputs larger
+// than a slot, communicators whose ranks could not all map each other's
+// regions, and processes without MQ_P2P_GATHER=1 use NCCL's all-gather.
 //
 // NCCL is loaded at the first mq_comm call with dlopen("libnccl.so.2"), so
 // the library has no link-time dependency on it and, inside a PyTorch
@@ -18,18 +35,27 @@
 #include <mutex>
 
 #include "mq_common.cuh"
+#include "mq_sm100.cuh"
 #include "mq_tcdec_api.h"
 
 #include "nccl.h"
 
 namespace mq {
 int gather_workspace_for(int device, cudaStream_t s, size_t bytes, void **out);
+int device_err_flag(int device, int **dev_ptr, int **host_ptr);
 void count_launch(int n);
+
+constexpr int kP2PMaxRanks = 8;
+constexpr size_t kP2PSlotFloats = size_t(1) << 20;  // 4 MiB per slot: m * rows_per_rank <= 1,048,576
+constexpr uint64_t kP2PWaitNs = 1000000000ull;
 }  // namespace mq
 
 struct mq_comm {
   int device = 0, nranks = 1, rank = 0;
   ncclComm_t comm = nullptr;
+  bool p2p = false;                           // peer-memory gather set up on every rank
+  char *stage = nullptr;                      // this rank's staging region
+  char *peer[mq::kP2PMaxRanks] = {nullptr};   // every rank's region as mapped here (own at [rank])
 };
 
 namespace mq {
@@ -82,6 +108,226 @@ __global__ void interleave_kernel(const float *__restrict__ g, int nranks, int m
   }
 }
 
+// Byte layout of a staging region: data [2][G][slot], flags [2][G] u32,
+// counters {epoch, push arrivals, pull arrivals} u32.
+__host__ __device__ inline size_t p2p_data_bytes(int G) { return 2 * (size_t)G * kP2PSlotFloats * sizeof(float); }
+__host__ __device__ inline size_t p2p_region_bytes(int G) { return p2p_data_bytes(G) + (2 * (size_t)G + 4) * 4; }
+
+struct P2PArgs {
+  float *y;          // the output [m, ldy]; this rank's slice at column rank * R
+  int64_t ldy;
+  int m, R, G, rank;
+  char *base[kP2PMaxRanks];
+  int *err;
+};
+
+__device__ __forceinline__ uint32_t *p2p_flags(char *base, int G) {
+  return reinterpret_cast<uint32_t *>(base + p2p_data_bytes(G));
+}
+__device__ __forceinline__ float *p2p_slot(char *base, int G, int half, int src) {
+  return reinterpret_cast<float *>(base) + ((size_t)half * G + src) * kP2PSlotFloats;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// This rank's slice [m, R] (row stride ldy) -> slot (half, rank) of every peer.
+template <bool VEC>
+__global__ void __launch_bounds__(256) p2p_push_kernel(const P2PArgs a) {
+  sm100::griddep_wait();  // the slice is the previous kernel's output
+  uint32_t *ctl = p2p_flags(a.base[a.rank], a.G) + 2 * a.G;
+  const uint32_t e = *reinterpret_cast<volatile uint32_t *>(&ctl[0]) + 1u;
+  const int half = (int)(e & 1u);
+  const float *src = a.y + (int64_t)a.rank * a.R;
+  const int64_t n = (int64_t)a.m * a.R;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int pp = 1; pp < a.G; ++pp) {
+    const int p = (a.rank + pp) % a.G;  // spread the peers' links over the CTAs' start order
+    float *dst = p2p_slot(a.base[p], a.G, half, a.rank);
+    if constexpr (VEC) {
+      const int rq = a.R / 4;
+      for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n / 4; i += stride) {
+        const int64_t c = i / rq, j = i % rq;
+        reinterpret_cast<float4 *>(dst)[i] = __ldcg(reinterpret_cast<const float4 *>(src + c * a.ldy + 4 * j));
+      }
+    } else {
+      for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        dst[i] = __ldcg(src + (i / a.R) * a.ldy + i % a.R);
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(&ctl[1], 1u) == gridDim.x - 1) {  // every CTA's stores are fenced
+    __threadfence_system();
+    for (int p = 0; p < a.G; ++p)
+      if (p != a.rank) st_release_sys(p2p_flags(a.base[p], a.G) + half * a.G + a.rank, e);
+    ctl[1] = 0u;
+  }
+}
+
+// Waits for every peer's slice of this epoch, then copies the peers' slots
+// into their columns of the output; the last CTA advances the epoch.
+template <bool VEC>
+__global__ void __launch_bounds__(256) p2p_pull_kernel(const P2PArgs a) {
+  __shared__ int s_ok;
+  char *mine = a.base[a.rank];
+  uint32_t *flags = p2p_flags(mine, a.G);
+  uint32_t *ctl = flags + 2 * a.G;
+  const uint32_t e = *reinterpret_cast<volatile uint32_t *>(&ctl[0]) + 1u;
+  const int half = (int)(e & 1u);
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const uint64_t t0 = sm100::globaltimer_ns();
+    for (int p = 0; p < a.G && ok; ++p) {
+      if (p == a.rank) continue;
+      for (uint32_t it = 0; ld_acquire_sys(flags + half * a.G + p) != e; ++it) {
+        if ((it & 63u) == 63u && sm100::globaltimer_ns() - t0 > kP2PWaitNs) {
+          ok = 0;
+          atomicExch(a.err, 1);
+          break;
+        }
+      }
+    }
+    __threadfence();
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (s_ok) {
+    const int64_t n = (int64_t)a.m * a.R;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int p = 0; p < a.G; ++p) {
+      if (p == a.rank) continue;
+      const float *slot = p2p_slot(mine, a.G, half, p);
+      float *dst = a.y + (int64_t)p * a.R;
+      if constexpr (VEC) {
+        const int rq = a.R / 4;
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n / 4; i += stride) {
+          const int64_t c = i / rq, j = i % rq;
+          *reinterpret_cast<float4 *>(dst + c * a.ldy + 4 * j) = __ldcg(reinterpret_cast<const float4 *>(slot) + i);
+        }
+      } else {
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+          dst[(i / a.R) * a.ldy + i % a.R] = __ldcg(slot + i);
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&ctl[2], 1u) == gridDim.x - 1) {
+      ctl[2] = 0u;
+      ctl[0] = e;  // the next call's epoch; the next kernels on the stream see it
+      __threadfence();
+    }
+  }
+}
+
+// Maps every rank's staging region on every rank; false (and nothing held)
+// unless all ranks succeeded.
+bool p2p_setup(mq_comm *c) {
+  const int G = c->nranks;
+  if (G < 2 || G > kP2PMaxRanks) return false;
+  const char *env = std::getenv("MQ_P2P_GATHER");  // opt-in: MQ_P2P_GATHER=1
+  if (!env || env[0] != '1') return false;
+  const size_t bytes = p2p_region_bytes(G);
+  bool ok = cudaMalloc(&c->stage, bytes) == cudaSuccess;
+  ok = ok && cudaMemset(c->stage, 0, bytes) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+  // Exchange {ok, handle} records over NCCL (in place: every rank sends its own record).
+  struct Rec {
+    int ok;
+    int pad[3];
+    cudaIpcMemHandle_t h;
+  };
+  Rec mine{};
+  mine.ok = ok && cudaIpcGetMemHandle(&mine.h, c->stage) == cudaSuccess;
+  Rec *d_recs = nullptr;
+  Rec recs[kP2PMaxRanks];
+  cudaStream_t s = nullptr;
+  bool ex = cudaMalloc(&d_recs, sizeof(Rec) * G) == cudaSuccess && cudaStreamCreate(&s) == cudaSuccess &&
+            cudaMemcpy(d_recs + c->rank, &mine, sizeof(Rec), cudaMemcpyHostToDevice) == cudaSuccess;
+  // Every rank takes part in the exchange, whatever its own state, so that no rank waits alone.
+  const ncclResult_t nr = nccl().all_gather(d_recs ? (const void *)(d_recs + c->rank) : nullptr, d_recs, sizeof(Rec),
+                                            ncclUint8, c->comm, s);
+  ex = ex && nr == ncclSuccess && cudaStreamSynchronize(s) == cudaSuccess &&
+       cudaMemcpy(recs, d_recs, sizeof(Rec) * G, cudaMemcpyDeviceToHost) == cudaSuccess;
+  if (s) cudaStreamDestroy(s);
+  if (d_recs) cudaFree(d_recs);
+  bool all = ex;
+  for (int p = 0; all && p < G; ++p) all = recs[p].ok != 0;
+  if (all) {
+    for (int p = 0; p < G; ++p) {
+      if (p == c->rank) {
+        c->peer[p] = c->stage;
+        continue;
+      }
+      void *q = nullptr;
+      if (cudaIpcOpenMemHandle(&q, recs[p].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        all = false;
+        break;
+      }
+      c->peer[p] = static_cast<char *>(q);
+    }
+  }
+  // Agree that every rank mapped every peer (a second exchange of one flag each).
+  int *d_ok = nullptr;
+  int oks[kP2PMaxRanks] = {0};
+  const int my_ok = all ? 1 : 0;
+  cudaStream_t s2 = nullptr;
+  bool ex2 = cudaMalloc(&d_ok, sizeof(int) * G) == cudaSuccess && cudaStreamCreate(&s2) == cudaSuccess &&
+             cudaMemcpy(d_ok + c->rank, &my_ok, sizeof(int), cudaMemcpyHostToDevice) == cudaSuccess;
+  const ncclResult_t nr2 =
+      nccl().all_gather(d_ok ? (const void *)(d_ok + c->rank) : nullptr, d_ok, 1, ncclInt32, c->comm, s2);
+  ex2 = ex2 && nr2 == ncclSuccess && cudaStreamSynchronize(s2) == cudaSuccess &&
+        cudaMemcpy(oks, d_ok, sizeof(int) * G, cudaMemcpyDeviceToHost) == cudaSuccess;
+  if (s2) cudaStreamDestroy(s2);
+  if (d_ok) cudaFree(d_ok);
+  bool agreed = ex2;
+  for (int p = 0; agreed && p < G; ++p) agreed = oks[p] != 0;
+  if (!agreed) {
+    for (int p = 0; p < G; ++p)
+      if (p != c->rank && c->peer[p]) cudaIpcCloseMemHandle(c->peer[p]);
+    for (int p = 0; p < G; ++p) c->peer[p] = nullptr;
+    if (c->stage) cudaFree(c->stage);
+    c->stage = nullptr;
+    cudaGetLastError();  // the fallback is NCCL: clear a failed call's error state
+    return false;
+  }
+  return true;
+}
+
+void p2p_release(mq_comm *c) {
+  if (!c->p2p) return;
+  for (int p = 0; p < c->nranks; ++p)
+    if (p != c->rank && c->peer[p]) cudaIpcCloseMemHandle(c->peer[p]);
+  if (c->stage) cudaFree(c->stage);
+  c->p2p = false;
+}
+
+// Launches the push kernel with programmatic stream serialization (it starts
+// while the decode kernel runs and waits for it with griddepcontrol.wait).
+template <bool VEC>
+cudaError_t p2p_launch(const P2PArgs &a, int grid, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, p2p_push_kernel<VEC>, a);
+  if (e != cudaSuccess) return e;
+  p2p_pull_kernel<VEC><<<grid, 256, 0, s>>>(a);
+  count_launch(2);
+  return cudaGetLastError();
+}
+
 }  // namespace
 }  // namespace mq
 
@@ -127,12 +373,22 @@ int mq_comm_create(int device, int nranks, int rank, const void *id, size_t len,
   c->nranks = nranks;
   c->rank = rank;
   c->comm = comm;
+  if ((e = cudaSetDevice(device)) == cudaSuccess) {
+    c->p2p = p2p_setup(c);
+    cudaSetDevice(prev);
+  }
   *out = c;
   return MQ_OK;
 }
 
 void mq_comm_destroy(mq_comm *c) {
   if (!c) return;
+  int prev = -1;
+  if (c->p2p && cudaGetDevice(&prev) == cudaSuccess && cudaSetDevice(c->device) == cudaSuccess) {
+    cudaDeviceSynchronize();
+    mq::p2p_release(c);
+    cudaSetDevice(prev);
+  }
   if (c->comm && mq::nccl().ok) mq::nccl().comm_destroy(c->comm);
   delete c;
 }
@@ -163,6 +419,19 @@ int mq_linear_sharded_allgather(const mq_weight *w, const float *x, int m, int l
   } restore{prev != w->device ? prev : -1};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const float *bias_slice = bias ? bias + (int64_t)r * R : nullptr;
+  if (comm->p2p && (size_t)m * R <= kP2PSlotFloats) {  // peer-memory gather
+    int *err_dev = nullptr, *err_host = nullptr;
+    int rc = device_err_flag(w->device, &err_dev, &err_host);
+    if (rc) return rc;
+    if ((rc = mq_linear(w, x, m, ldx, bias_slice, y + (int64_t)r * R, ldy, stream))) return rc;
+    P2PArgs a{y, (int64_t)ldy, m, R, G, r, {}, err_dev};
+    for (int p = 0; p < G; ++p) a.base[p] = comm->peer[p];
+    const bool vec = R % 4 == 0 && ldy % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+    const int64_t n = (int64_t)m * R / (vec ? 4 : 1);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148));
+    e = vec ? p2p_launch<true>(a, grid, s) : p2p_launch<false>(a, grid, s);
+    return e == cudaSuccess ? MQ_OK : cuda_fail(e, "peer gather launch");
+  }
   if (m == 1) {  // y is [G*R] contiguous: in-place gather straight into it
     float *mine = y + (int64_t)r * R;
     int rc = mq_linear(w, x, 1, ldx, bias_slice, mine, R, stream);

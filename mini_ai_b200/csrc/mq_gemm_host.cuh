@@ -209,6 +209,10 @@ cudaError_t launch_gemm_t(const CUtensorMap &th, const CUtensorMap &tl, const Ge
 
 }  // namespace
 
+// The device's bounded-wait error flag, for kernels launched from other files
+// (the peer-memory gather of the row-sharded linear).
+int device_err_flag(int device, int **dev_ptr, int **host_ptr) { return err_flag(device, dev_ptr, host_ptr); }
+
 int env_threshold(const char *name, int dflt) {
   const char *e = std::getenv(name);
   return e && *e ? std::atoi(e) : dflt;

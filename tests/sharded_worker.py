@@ -47,6 +47,35 @@ def main() -> int:
                     print(f"rank {rank}: sharded != unsharded (type {q}, m {m})", flush=True)
                     return 1
                 assert_linear_close(a, orc.linear(q, s.bytes, rows, cols, xn), abs_dot_bound(deq, xn))
+            # Consecutive calls into one output (the gather alternates its two
+            # staging halves), then the same calls captured in a CUDA graph and
+            # replayed with new inputs (the gather's epoch lives on the device).
+            for m in (1, 16):
+                xs = torch.from_numpy(rng.standard_normal((3, m, cols)).astype(np.float32)).cuda(dev)
+                out = torch.empty((m, rows), dtype=torch.float32, device=f"cuda:{dev}")
+                for i in range(3):
+                    sl.linear(xs[i], out=out)
+                    if not torch.equal(out, full.linear(xs[i])):
+                        print(f"rank {rank}: consecutive call {i} differs (type {q}, m {m})", flush=True)
+                        return 1
+                st = torch.cuda.Stream(dev)
+                xin = torch.empty((m, cols), dtype=torch.float32, device=f"cuda:{dev}")
+                with torch.cuda.stream(st):
+                    sl.linear(xin.copy_(xs[0]), out=out, stream=st)  # eager call on the capture stream first
+                torch.cuda.synchronize(dev)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=st):
+                    sl.linear(xin, out=out, stream=st)
+                    sl.linear(xin, out=out, stream=st)
+                for i in (1, 2):
+                    xin.copy_(xs[i])
+                    torch.cuda.synchronize(dev)
+                    graph.replay()
+                    torch.cuda.synchronize(dev)
+                    if not torch.equal(out, full.linear(xs[i])):
+                        print(f"rank {rank}: graph replay {i} differs (type {q}, m {m})", flush=True)
+                        return 1
+                del graph
             sl.close()
             full.close()
         comm.close()

@@ -128,13 +128,15 @@ def test_single_rank_nccl_path_matches_linear(mq, oracle, cuda_device, q):
 
 
 @pytest.mark.gpu
-def test_two_ranks_nccl_allgather():
-    """Two processes on two GPUs through torchrun (skipped on one-GPU boxes)."""
+@pytest.mark.parametrize("gather", ["peer", "nccl"])
+def test_two_ranks_allgather(gather):
+    """Two processes on two GPUs through torchrun (skipped on one-GPU boxes): the
+    peer-memory gather (MQ_P2P_GATHER=1) and NCCL's all-gather."""
     import torch
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MQ_P2P_GATHER="1" if gather == "peer" else "0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1",
            f"--master-port={_free_port()}", str(ROOT / "tests" / "sharded_worker.py")]
     res = subprocess.run(["timeout", "-k", "30", "300", *cmd], capture_output=True, text=True, env=env, cwd=ROOT)
