@@ -119,6 +119,17 @@ int mq_weight_export(const mq_weight *w, void *dst, size_t dst_bytes);
 int mq_linear(const mq_weight *w, const float *x, int m, int ldx, const float *bias, float *y, int ldy,
               void *stream);
 
+/* The gate/up half of the Llama FFN in one call: y = SwiGlu(x * W_gateᵀ,
+ * x * W_upᵀ), i.e. y[i, n] = g / (1 + exp(-g)) * u with g, u the two products,
+ * as FfnForward's `Linear(h, w_gate)`, `Linear(h, w_up)`, `SwiGlu(gate, up)`
+ * (src/forward.cc:105-110; SwiGluKernel, src/cuda_backend.cu:241-245; Silu,
+ * src/ops.cc:85-91). The gate product goes to a per-(device, stream) scratch
+ * buffer and the up product's kernel applies the SwiGLU in its output write,
+ * so the separate elementwise pass and one round trip of both outputs are
+ * gone. Both weights must have the same shape and device; x, y as mq_linear. */
+int mq_linear_swiglu(const mq_weight *w_gate, const mq_weight *w_up, const float *x, int m, int ldx, float *y,
+                     int ldy, void *stream);
+
 /* Same product for a ragged batch: `offsets` (host, n_seqs + 1 entries,
  * offsets[0] == 0, non-decreasing) delimits each request's rows inside the
  * contiguous [offsets[n_seqs], ldx] activation matrix. The rows are

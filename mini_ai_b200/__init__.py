@@ -5,11 +5,12 @@ this package is the host-side mirror of the reference operator surface over it.
 """
 from ._lib import LIB_PATH, MQError, lib
 from .quantized_tensor import (BlockBytes, CudaDeviceInfo, CudaWeight, DequantizeTensor, Linear, LinearDispatch,
-                               QuantizedStorage, QuantizeTensor, QuantType, TensorFromQuantized, set_path)
+                               LinearSwiGlu, QuantizedStorage, QuantizeTensor, QuantType, TensorFromQuantized,
+                               set_path)
 from .sharded import CudaComm, ShardedLinear, assemble, shard_rows
 
 __all__ = [
     "LIB_PATH", "MQError", "lib", "BlockBytes", "CudaDeviceInfo", "CudaWeight", "DequantizeTensor", "Linear",
-    "LinearDispatch", "QuantizedStorage", "QuantizeTensor", "QuantType", "TensorFromQuantized", "set_path",
+    "LinearDispatch", "LinearSwiGlu", "QuantizedStorage", "QuantizeTensor", "QuantType", "TensorFromQuantized", "set_path",
     "CudaComm", "ShardedLinear", "assemble", "shard_rows",
 ]

@@ -110,6 +110,27 @@ int quantize_host(int qtype, const float *src, int rows, int cols, uint8_t *dst,
 
 using namespace mq;
 
+namespace mq {
+namespace {
+
+// The kernel choice of mq_linear; `gate` ([m, ldy], optional) turns the output
+// write into the SwiGLU epilogue of the fused gate/up product.
+int linear_dispatch(const mq_weight *w, const float *x, int m, int ldx, const float *bias, float *y, int ldy,
+                    cudaStream_t s, const float *gate) {
+  const int mode = g_path_mode;
+  if (!gemm_supported(w->device))
+    return fail(MQ_ERR_UNSUPPORTED, "the kernels need an sm_100 device (device %d)", w->device);
+  if (mode == 1) return run_sdec(w, x, m, ldx, bias, y, ldy, s, gate);
+  if (mode == 3) return run_i8dec(w, x, m, ldx, bias, y, ldy, s, gate);
+  if (mode == 4) return run_tcdec(w, x, m, ldx, bias, y, ldy, s, gate);
+  if (mode == 2 || (mode == 0 && m > decode_max_m())) return run_gemm(w, x, m, ldx, bias, y, ldy, s, gate);
+  if (m <= i8dec_max_m()) return run_i8dec(w, x, m, ldx, bias, y, ldy, s, gate);
+  return run_tcdec(w, x, m, ldx, bias, y, ldy, s, gate);
+}
+
+}  // namespace
+}  // namespace mq
+
 extern "C" {
 
 const char *mq_last_error(void) { return last_error().c_str(); }
@@ -308,16 +329,33 @@ int mq_linear(const mq_weight *w, const float *x, int m, int ldx, const float *b
   if (ldy < w->v.rows) return fail(MQ_ERR_INVALID, "output stride %d < rows %d", ldy, w->v.rows);
   DeviceGuard g(w->device);
   if (g.err != cudaSuccess) return cuda_fail(g.err, "cudaSetDevice");
+  return linear_dispatch(w, x, m, ldx, bias, y, ldy, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int mq_linear_swiglu(const mq_weight *w_gate, const mq_weight *w_up, const float *x, int m, int ldx, float *y,
+                     int ldy, void *stream) {
+  last_error().clear();
+  if (!w_gate || !w_up) return fail(MQ_ERR_INVALID, "null weight handle");
+  if (w_gate->device != w_up->device)
+    return fail(MQ_ERR_INVALID, "gate on device %d, up on device %d", w_gate->device, w_up->device);
+  if (w_gate->v.rows != w_up->v.rows || w_gate->v.cols != w_up->v.cols)
+    return fail(MQ_ERR_INVALID, "SwiGlu: shape mismatch (gate %dx%d, up %dx%d)", w_gate->v.rows, w_gate->v.cols,
+                w_up->v.rows, w_up->v.cols);
+  if (m < 0) return fail(MQ_ERR_INVALID, "negative activation count %d", m);
+  if (m == 0) return MQ_OK;
+  if (!x || !y) return fail(MQ_ERR_INVALID, "null activation or output pointer");
+  if (ldx < w_up->v.cols)
+    return fail(MQ_ERR_INVALID, "LinearDispatch: dimension mismatch (ldx %d < cols %d)", ldx, w_up->v.cols);
+  if (ldy < w_up->v.rows) return fail(MQ_ERR_INVALID, "output stride %d < rows %d", ldy, w_up->v.rows);
+  DeviceGuard g(w_up->device);
+  if (g.err != cudaSuccess) return cuda_fail(g.err, "cudaSetDevice");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int mode = g_path_mode;
-  if (!gemm_supported(w->device))
-    return fail(MQ_ERR_UNSUPPORTED, "the kernels need an sm_100 device (device %d)", w->device);
-  if (mode == 1) return run_sdec(w, x, m, ldx, bias, y, ldy, s);
-  if (mode == 3) return run_i8dec(w, x, m, ldx, bias, y, ldy, s);
-  if (mode == 4) return run_tcdec(w, x, m, ldx, bias, y, ldy, s);
-  if (mode == 2 || (mode == 0 && m > decode_max_m())) return run_gemm(w, x, m, ldx, bias, y, ldy, s);
-  if (m <= i8dec_max_m()) return run_i8dec(w, x, m, ldx, bias, y, ldy, s);
-  return run_tcdec(w, x, m, ldx, bias, y, ldy, s);
+  void *ws = nullptr;  // the gate product, laid out like y ([m, ldy])
+  int rc = gate_workspace_for(w_up->device, s, (size_t)m * ldy * sizeof(float), &ws);
+  if (rc) return rc;
+  float *gate = static_cast<float *>(ws);
+  if ((rc = linear_dispatch(w_gate, x, m, ldx, nullptr, gate, ldy, s, nullptr))) return rc;
+  return linear_dispatch(w_up, x, m, ldx, nullptr, y, ldy, s, gate);
 }
 
 int mq_linear_ragged(const mq_weight *w, const float *x, const int *offsets, int n_seqs, int ldx, const float *bias,

@@ -95,6 +95,15 @@ __host__ __device__ inline int pk_byte_off(int qtype, int r, int jb, int i) {
 }
 
 // Chunk of (tile t, step k); scales of row r at + pk_bytes + 16 r, mins at + pk_bytes + 2048 + 16 r.
+// Output epilogue of the fused gate/up product (the reference's SwiGluKernel,
+// src/cuda_backend.cu:241-245, applied to the up product's output): with a
+// gate buffer of the same layout as y, y = g / (1 + exp(-g)) * v; without, v.
+__device__ __forceinline__ float swiglu_out(float v, const float *gate, int64_t idx) {
+  if (!gate) return v;
+  const float g = gate[idx];
+  return g / (1.0f + expf(-g)) * v;
+}
+
 __host__ __device__ inline const uint8_t *chunk_ptr(const WeightView &w, int t, int k) {
   return w.base + ((int64_t)t * w.steps + k) * w.chunk_bytes;
 }

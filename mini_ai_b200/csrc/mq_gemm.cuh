@@ -44,6 +44,7 @@ struct GemmArgs {
   int m;         // activation rows
   int ktiles;    // ceil(nb / 2) K steps of 64
   int *err;      // device-visible error flag
+  const float *gate = nullptr;  // fused gate/up product: y = silu(gate) * (product + bias); gate [m, ldy]
 };
 
 // x (fp32, [m, ldx]) -> xh, xl (bf16, [m, kpad]); columns >= K are zero.
@@ -288,7 +289,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const int mm = m0 + c0 + j;
-          if (mm < a.m) a.y[(int64_t)mm * a.ldy + n] = __uint_as_float(v[j]) + bias;
+          if (mm < a.m) a.y[(int64_t)mm * a.ldy + n] = swiglu_out(__uint_as_float(v[j]) + bias, a.gate, (int64_t)mm * a.ldy + n);
         }
       }
     }
@@ -306,11 +307,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 int decode_max_m();
 int sdec_max_m();
 bool gemm_supported(int device);
+// gate: optional [m, ldy] buffer of the fused gate/up product (y = silu(gate) * product).
 int run_sdec(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-             cudaStream_t s);
+             cudaStream_t s, const float *gate = nullptr);
 int run_tcdec(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-              cudaStream_t s);
+              cudaStream_t s, const float *gate = nullptr);
 int run_gemm(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-             cudaStream_t s);
+             cudaStream_t s, const float *gate = nullptr);
 
 }  // namespace mq

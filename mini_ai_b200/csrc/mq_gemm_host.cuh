@@ -68,6 +68,26 @@ int gather_workspace_for(int device, cudaStream_t s, size_t bytes, void **out) {
   return MQ_OK;
 }
 
+// Gate-product buffer of mq_linear_swiglu, one per (device, stream).
+std::map<std::pair<int, cudaStream_t>, Workspace> g_gate;
+
+int gate_workspace_for(int device, cudaStream_t s, size_t bytes, void **out) {
+  std::lock_guard<std::mutex> lock(g_ws_mu);
+  Workspace &w = g_gate[{device, s}];
+  if (w.bytes < bytes) {
+    if (w.ptr) {
+      MQ_CUDA(cudaStreamSynchronize(s));
+      MQ_CUDA(cudaFree(w.ptr));
+      w.ptr = nullptr;
+      w.bytes = 0;
+    }
+    MQ_CUDA(cudaMalloc(&w.ptr, bytes));
+    w.bytes = bytes;
+  }
+  *out = w.ptr;
+  return MQ_OK;
+}
+
 namespace {
 
 // Split-K fixup tickets, one zeroed array per (device, stream); each launch
@@ -267,7 +287,7 @@ DecPlan tcdec_plan(const WeightView &w, int device, int max_grid) {
 }
 
 int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const float *bias, float *y, int64_t ldy,
-                 cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort) {
+                 cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort, const float *gate) {
   const int bn = dec_tile_rows(mm);
   MQ_CUDA(launch_pdl(dec_prep_kernel, dim3(plan.steps, (bn + 7) / 8), dim3(256), 0, s, x, ldx, mm, w.cols, plan.kpad,
                      bn, buf.x2, buf.xsum, buf.xinv, (int)(w.qtype == MQ_Q4_1)));
@@ -277,7 +297,7 @@ int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const
   if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf.x2, 2 * bn, plan.kpad, plan.kpad, 64, 2 * bn)))
     return rc;
   DecArgs a{w, mm, buf.xinv, buf.xsum, bias, y, ldy, buf.partial, buf.tickets, plan.steps, plan.tiles, buf.err,
-            nan_on_abort};
+            nan_on_abort, gate};
   cudaError_t e;
   switch (w.qtype) {
   case MQ_Q8_0: e = launch_tcdec_q<MQ_Q8_0>(tx, a, plan.grid, mm, s); break;
@@ -290,7 +310,7 @@ int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const
 
 // tcgen05 decode GEMM: up to 32 activation rows per launch (split + kernel).
 int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-              cudaStream_t s) {
+              cudaStream_t s, const float *gate) {
   int *err_dev = nullptr, *err_host = nullptr;
   int rc = err_flag(wt->device, &err_dev, &err_host);
   if (rc) return rc;
@@ -319,7 +339,8 @@ int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
     buf.partial = reinterpret_cast<float *>(base + ((xbytes + sbytes + ibytes + 1023) & ~size_t(1023)));
     buf.tickets = tickets;
     buf.err = err_dev;
-    if ((rc = tcdec_launch(w, x + (int64_t)i0 * ldx, mm, ldx, bias, y + (int64_t)i0 * ldy, ldy, s, plan, buf, 0)))
+    if ((rc = tcdec_launch(w, x + (int64_t)i0 * ldx, mm, ldx, bias, y + (int64_t)i0 * ldy, ldy, s, plan, buf, 0,
+                           gate ? gate + (int64_t)i0 * ldy : nullptr)))
       return rc;
   }
   return MQ_OK;
@@ -360,7 +381,7 @@ int sdec_max_m() {
 // are read by TMA straight from x when its base and row stride are 16-byte
 // aligned; otherwise they are first copied to an aligned scratch.
 int run_sdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-             cudaStream_t s) {
+             cudaStream_t s, const float *gate) {
   int *err_dev = nullptr, *err_host = nullptr;
   int rc = err_flag(wt->device, &err_dev, &err_host);
   if (rc) return rc;
@@ -400,7 +421,7 @@ int run_sdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const floa
                         CU_TENSOR_MAP_SWIZZLE_NONE)))
       return rc;
     SdecArgs a{w, mm, bias, y + (int64_t)i0 * ldy, ldy, reinterpret_cast<float *>(base), tickets, plan.steps,
-               plan.tiles, err_dev, 0};
+               plan.tiles, err_dev, 0, gate ? gate + (int64_t)i0 * ldy : nullptr};
     cudaError_t e;
     switch (w.qtype) {
     case MQ_Q8_0: e = launch_sdec_q<MQ_Q8_0>(tx, a, plan.grid, mc, s); break;
@@ -446,7 +467,7 @@ int i8dec_max_m() {
 
 // int8 tensor-core decode: up to 4 activation rows per launch.
 int run_i8dec(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-              cudaStream_t s) {
+              cudaStream_t s, const float *gate = nullptr) {
   int *err_dev = nullptr, *err_host = nullptr;
   int rc = err_flag(wt->device, &err_dev, &err_host);
   if (rc) return rc;
@@ -465,7 +486,7 @@ int run_i8dec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
     void *ws = nullptr;
     if ((rc = workspace_for(wt->device, s, pbytes + 1024, &ws))) return rc;
     I8Args a{w, mm, x + (int64_t)i0 * ldx, ldx, bias, y + (int64_t)i0 * ldy, ldy, static_cast<float *>(ws), tickets,
-             plan.steps, plan.tiles, err_dev, 0};
+             plan.steps, plan.tiles, err_dev, 0, gate ? gate + (int64_t)i0 * ldy : nullptr};
     cudaError_t e;
     switch (w.qtype) {
     case MQ_Q8_0: e = launch_i8dec_q<MQ_Q8_0>(a, plan.grid, mc, s); break;
@@ -478,7 +499,7 @@ int run_i8dec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
 }
 
 int run_gemm(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-             cudaStream_t s) {
+             cudaStream_t s, const float *gate) {
   int *err_dev = nullptr, *err_host = nullptr;
   int rc = err_flag(wt->device, &err_dev, &err_host);
   if (rc) return rc;
@@ -503,7 +524,7 @@ int run_gemm(const mq_weight *wt, const float *x, int m, int64_t ldx, const floa
   CUtensorMap th, tl;
   if ((rc = make_tmap_bf16(&th, xh, m, kpad, BN))) return rc;
   if ((rc = make_tmap_bf16(&tl, xl, m, kpad, BN))) return rc;
-  GemmArgs a{w, y, ldy, bias, m, (w.nb + 1) / 2, err_dev};
+  GemmArgs a{w, y, ldy, bias, m, (w.nb + 1) / 2, err_dev, gate};
   cudaError_t e;
   switch (w.qtype) {
   case MQ_Q8_0: e = launch_gemm_t<MQ_Q8_0, BN, STAGES>(th, tl, a, s); break;

@@ -211,6 +211,29 @@ class CudaWeight:
             pass
 
 
+def LinearSwiGlu(x, w_gate: CudaWeight, w_up: CudaWeight, out=None, stream=None):
+    """SwiGlu(Linear(x, w_gate), Linear(x, w_up)) in one call (FfnForward's gate/up half,
+    src/forward.cc:105-110, with SwiGluKernel, src/cuda_backend.cu:241-245)."""
+    torch = _torch()
+    if x.dtype != torch.float32 or not x.is_cuda:
+        raise RuntimeError("Linear requires F32 activations on the weight's device")
+    squeeze = x.dim() == 1
+    x2 = x.unsqueeze(0) if squeeze else x
+    if x2.dim() != 2 or x2.shape[1] != w_up.cols:
+        raise RuntimeError("LinearDispatch: dimension mismatch")
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    m, n = x2.shape[0], w_up.rows
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    elif out.shape[-1] != n or out.dtype != torch.float32:
+        raise RuntimeError("output shape mismatch")
+    out2 = out.view(m, n) if out.dim() == 1 else out
+    check(lib().mq_linear_swiglu(w_gate.handle, w_up.handle, x2.data_ptr(), m, x2.stride(0), out2.data_ptr(),
+                                 out2.stride(0), _stream_handle(stream)), "SwiGlu")
+    return out2.view(n) if squeeze and out.dim() != 1 else out
+
+
 def LinearDispatch(x, weight: CudaWeight, bias=None):
     """Quantized branch of LinearDispatch (src/matmul_optimized.cc:146-182) on the GPU."""
     return weight.linear(x, bias=bias)

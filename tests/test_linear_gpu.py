@@ -245,3 +245,56 @@ def test_prefill_ragged_q8_0_rows_checked(mq, oracle, cuda_device):
         bound = abs_dot_bound(oracle.dequantize(Q8_0, sub, len(pick), cols), x)
         assert_linear_close(y[:, pick], y_ref, bound)
         torch.cuda.synchronize()
+
+
+def _silu(v):
+    return v / (1.0 + np.exp(-v))
+
+
+@pytest.mark.parametrize("path", [0] + sorted(PATHS), ids=lambda p: PATHS.get(p, "automatic"))
+@pytest.mark.parametrize("q", QTYPES, ids=lambda q: NAMES[q])
+def test_swiglu_gate_up_against_oracle(mq, oracle, cuda_device, path, q):
+    """mq_linear_swiglu = SwiGlu(Linear(x, w_gate), Linear(x, w_up)) (src/forward.cc:105-110,
+    SwiGluKernel src/cuda_backend.cu:241-245) through every kernel's output epilogue, on odd
+    shapes (tail blocks, row tails) and activation counts across the automatic path's regimes.
+    Tolerance: the linear parity bound carried through silu (|silu'| < 1.1)."""
+    torch = _torch()
+    ms = {0: [1, 3, 16, 40], 1: [1, 3, 5], 3: [1, 2, 4, 5], 4: [1, 5, 16, 33], 2: [1, 129]}[path]
+    for rows, cols in [(300, 4097), (1024, 4096)]:
+        for m in ms:
+            sg, x, g_ref, bg = _llama_case(mq, oracle, q, rows, cols, m, seed=rows * 3 + m + path * 11)
+            su, _, _, _ = _llama_case(mq, oracle, q, rows, cols, m, seed=rows * 5 + m + path * 13)
+            u_ref = oracle.linear(q, su.bytes, rows, cols, x, threads=THREADS)
+            bu = abs_dot_bound(oracle.dequantize(q, su.bytes, rows, cols), x)
+            g64, u64 = g_ref.astype(np.float64), u_ref.astype(np.float64)
+            ref = _silu(g64) * u64
+            bound = 1.1 * bg * np.abs(u64) + np.abs(_silu(g64)) * bu
+            wg, wu = mq.CudaWeight(sg, device=cuda_device), mq.CudaWeight(su, device=cuda_device)
+            prev = mq.set_path(path)
+            try:
+                y = mq.LinearSwiGlu(dev(x, cuda_device), wg, wu)
+                # the same two products, unfused, with the reference's elementwise SwiGLU
+                g = wg.linear(dev(x, cuda_device))
+                u = wu.linear(dev(x, cuda_device))
+                torch.cuda.synchronize(cuda_device)
+            finally:
+                mq.set_path(prev)
+            assert_linear_close(y.cpu().numpy(), ref, bound)
+            unfused = (g / (1.0 + torch.exp(-g)) * u).cpu().numpy()
+            np.testing.assert_allclose(y.cpu().numpy(), unfused, rtol=2e-6, atol=1e-7)
+            wg.close()
+            wu.close()
+
+
+def test_swiglu_validation(mq, cuda_device):
+    """Shape and device mismatches are rejected before any launch."""
+    rng = np.random.default_rng(5)
+    a = mq.QuantizeTensor((rng.standard_normal((256, 128)) * 0.02).astype(np.float32), Q4_0)
+    b = mq.QuantizeTensor((rng.standard_normal((128, 128)) * 0.02).astype(np.float32), Q4_0)
+    wa, wb = mq.CudaWeight(a, device=cuda_device), mq.CudaWeight(b, device=cuda_device)
+    with pytest.raises(mq.MQError, match="shape mismatch"):
+        mq.LinearSwiGlu(dev(np.zeros((1, 128), np.float32), cuda_device), wa, wb)
+    with pytest.raises(RuntimeError, match="dimension mismatch"):
+        mq.LinearSwiGlu(dev(np.zeros((1, 64), np.float32), cuda_device), wa, wa)
+    wa.close()
+    wb.close()
