@@ -130,6 +130,14 @@ int mq_linear(const mq_weight *w, const float *x, int m, int ldx, const float *b
 int mq_linear_swiglu(const mq_weight *w_gate, const mq_weight *w_up, const float *x, int m, int ldx, float *y,
                      int ldy, void *stream);
 
+/* y = residual + (x * Wᵀ + bias): the linear followed by the residual add of
+ * ForwardCuda (`AddKernel(x, o)` after the wo and w_down projections,
+ * src/cuda_backend.cu:236-240), in the kernel's own output write. residual:
+ * device F32 [m, ldy] with y's stride; it may be y itself (the usual
+ * in-place residual stream). Otherwise as mq_linear. */
+int mq_linear_residual(const mq_weight *w, const float *x, int m, int ldx, const float *bias, const float *residual,
+                       float *y, int ldy, void *stream);
+
 /* Same product for a ragged batch: `offsets` (host, n_seqs + 1 entries,
  * offsets[0] == 0, non-decreasing) delimits each request's rows inside the
  * contiguous [offsets[n_seqs], ldx] activation matrix. The rows are

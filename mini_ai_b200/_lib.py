@@ -39,6 +39,7 @@ SIGNATURES = {
     "mq_linear_ragged": (_i, [_vp, _vp, C.POINTER(_i), _i, _i, _vp, _vp, _i, _vp]),
     "mq_linear_noalloc": (_i, [_vp, _vp, _i, _i, _vp, _vp, _i, _vp]),
     "mq_linear_swiglu": (_i, [_vp, _vp, _vp, _i, _i, _vp, _i, _vp]),
+    "mq_linear_residual": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp, _i, _vp]),
     "mq_comm_unique_id": (_i, [_vp, _sz]),
     "mq_comm_create": (_i, [_i, _i, _i, _vp, _sz, C.POINTER(_vp)]),
     "mq_comm_destroy": (None, [_vp]),

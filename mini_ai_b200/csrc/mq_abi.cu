@@ -113,19 +113,20 @@ using namespace mq;
 namespace mq {
 namespace {
 
-// The kernel choice of mq_linear; `gate` ([m, ldy], optional) turns the output
-// write into the SwiGLU epilogue of the fused gate/up product.
+// The kernel choice of mq_linear; `gate` and `resid` ([m, ldy], optional) turn
+// the output write into the SwiGLU epilogue of the fused gate/up product and
+// the residual add.
 int linear_dispatch(const mq_weight *w, const float *x, int m, int ldx, const float *bias, float *y, int ldy,
-                    cudaStream_t s, const float *gate) {
+                    cudaStream_t s, const float *gate, const float *resid) {
   const int mode = g_path_mode;
   if (!gemm_supported(w->device))
     return fail(MQ_ERR_UNSUPPORTED, "the kernels need an sm_100 device (device %d)", w->device);
-  if (mode == 1) return run_sdec(w, x, m, ldx, bias, y, ldy, s, gate);
-  if (mode == 3) return run_i8dec(w, x, m, ldx, bias, y, ldy, s, gate);
-  if (mode == 4) return run_tcdec(w, x, m, ldx, bias, y, ldy, s, gate);
-  if (mode == 2 || (mode == 0 && m > decode_max_m())) return run_gemm(w, x, m, ldx, bias, y, ldy, s, gate);
-  if (m <= i8dec_max_m()) return run_i8dec(w, x, m, ldx, bias, y, ldy, s, gate);
-  return run_tcdec(w, x, m, ldx, bias, y, ldy, s, gate);
+  if (mode == 1) return run_sdec(w, x, m, ldx, bias, y, ldy, s, gate, resid);
+  if (mode == 3) return run_i8dec(w, x, m, ldx, bias, y, ldy, s, gate, resid);
+  if (mode == 4) return run_tcdec(w, x, m, ldx, bias, y, ldy, s, gate, resid);
+  if (mode == 2 || (mode == 0 && m > decode_max_m())) return run_gemm(w, x, m, ldx, bias, y, ldy, s, gate, resid);
+  if (m <= i8dec_max_m()) return run_i8dec(w, x, m, ldx, bias, y, ldy, s, gate, resid);
+  return run_tcdec(w, x, m, ldx, bias, y, ldy, s, gate, resid);
 }
 
 }  // namespace
@@ -329,7 +330,21 @@ int mq_linear(const mq_weight *w, const float *x, int m, int ldx, const float *b
   if (ldy < w->v.rows) return fail(MQ_ERR_INVALID, "output stride %d < rows %d", ldy, w->v.rows);
   DeviceGuard g(w->device);
   if (g.err != cudaSuccess) return cuda_fail(g.err, "cudaSetDevice");
-  return linear_dispatch(w, x, m, ldx, bias, y, ldy, static_cast<cudaStream_t>(stream), nullptr);
+  return linear_dispatch(w, x, m, ldx, bias, y, ldy, static_cast<cudaStream_t>(stream), nullptr, nullptr);
+}
+
+int mq_linear_residual(const mq_weight *w, const float *x, int m, int ldx, const float *bias, const float *residual,
+                       float *y, int ldy, void *stream) {
+  last_error().clear();
+  if (!w) return fail(MQ_ERR_INVALID, "null weight handle");
+  if (m < 0) return fail(MQ_ERR_INVALID, "negative activation count %d", m);
+  if (m == 0) return MQ_OK;
+  if (!x || !y || !residual) return fail(MQ_ERR_INVALID, "null activation, residual or output pointer");
+  if (ldx < w->v.cols) return fail(MQ_ERR_INVALID, "LinearDispatch: dimension mismatch (ldx %d < cols %d)", ldx, w->v.cols);
+  if (ldy < w->v.rows) return fail(MQ_ERR_INVALID, "output stride %d < rows %d", ldy, w->v.rows);
+  DeviceGuard g(w->device);
+  if (g.err != cudaSuccess) return cuda_fail(g.err, "cudaSetDevice");
+  return linear_dispatch(w, x, m, ldx, bias, y, ldy, static_cast<cudaStream_t>(stream), nullptr, residual);
 }
 
 int mq_linear_swiglu(const mq_weight *w_gate, const mq_weight *w_up, const float *x, int m, int ldx, float *y,
@@ -354,8 +369,8 @@ int mq_linear_swiglu(const mq_weight *w_gate, const mq_weight *w_up, const float
   int rc = gate_workspace_for(w_up->device, s, (size_t)m * ldy * sizeof(float), &ws);
   if (rc) return rc;
   float *gate = static_cast<float *>(ws);
-  if ((rc = linear_dispatch(w_gate, x, m, ldx, nullptr, gate, ldy, s, nullptr))) return rc;
-  return linear_dispatch(w_up, x, m, ldx, nullptr, y, ldy, s, gate);
+  if ((rc = linear_dispatch(w_gate, x, m, ldx, nullptr, gate, ldy, s, nullptr, nullptr))) return rc;
+  return linear_dispatch(w_up, x, m, ldx, nullptr, y, ldy, s, gate, nullptr);
 }
 
 int mq_linear_ragged(const mq_weight *w, const float *x, const int *offsets, int n_seqs, int ldx, const float *bias,

@@ -95,13 +95,18 @@ __host__ __device__ inline int pk_byte_off(int qtype, int r, int jb, int i) {
 }
 
 // Chunk of (tile t, step k); scales of row r at + pk_bytes + 16 r, mins at + pk_bytes + 2048 + 16 r.
-// Output epilogue of the fused gate/up product (the reference's SwiGluKernel,
-// src/cuda_backend.cu:241-245, applied to the up product's output): with a
-// gate buffer of the same layout as y, y = g / (1 + exp(-g)) * v; without, v.
-__device__ __forceinline__ float swiglu_out(float v, const float *gate, int64_t idx) {
-  if (!gate) return v;
-  const float g = gate[idx];
-  return g / (1.0f + expf(-g)) * v;
+// Output epilogues, both on buffers laid out like y ([m, ldy]): the fused
+// gate/up product (the reference's SwiGluKernel, src/cuda_backend.cu:241-245,
+// applied to the up product's output): y = g / (1 + exp(-g)) * v; and the
+// residual add (AddKernel, src/cuda_backend.cu:236-240): y = r + v, r may be
+// y itself (each element is read and written by the same thread once).
+__device__ __forceinline__ float epilogue_out(float v, const float *gate, const float *resid, int64_t idx) {
+  if (gate) {
+    const float g = gate[idx];
+    v = g / (1.0f + expf(-g)) * v;
+  }
+  if (resid) v = resid[idx] + v;
+  return v;
 }
 
 __host__ __device__ inline const uint8_t *chunk_ptr(const WeightView &w, int t, int k) {

@@ -44,7 +44,8 @@ struct GemmArgs {
   int m;         // activation rows
   int ktiles;    // ceil(nb / 2) K steps of 64
   int *err;      // device-visible error flag
-  const float *gate = nullptr;  // fused gate/up product: y = silu(gate) * (product + bias); gate [m, ldy]
+  const float *gate = nullptr;   // fused gate/up product: y = silu(gate) * (product + bias); gate [m, ldy]
+  const float *resid = nullptr;  // residual add: y = resid + (product + bias); resid [m, ldy], may be y
 };
 
 // x (fp32, [m, ldx]) -> xh, xl (bf16, [m, kpad]); columns >= K are zero.
@@ -289,7 +290,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const int mm = m0 + c0 + j;
-          if (mm < a.m) a.y[(int64_t)mm * a.ldy + n] = swiglu_out(__uint_as_float(v[j]) + bias, a.gate, (int64_t)mm * a.ldy + n);
+          if (mm < a.m) a.y[(int64_t)mm * a.ldy + n] = epilogue_out(__uint_as_float(v[j]) + bias, a.gate, a.resid, (int64_t)mm * a.ldy + n);
         }
       }
     }
@@ -307,12 +308,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 int decode_max_m();
 int sdec_max_m();
 bool gemm_supported(int device);
-// gate: optional [m, ldy] buffer of the fused gate/up product (y = silu(gate) * product).
+// gate, resid: optional [m, ldy] buffers of the output epilogues (fused
+// gate/up product: y = silu(gate) * product; residual add: y = resid + product).
 int run_sdec(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-             cudaStream_t s, const float *gate = nullptr);
+             cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr);
 int run_tcdec(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-              cudaStream_t s, const float *gate = nullptr);
+              cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr);
 int run_gemm(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-             cudaStream_t s, const float *gate = nullptr);
+             cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr);
 
 }  // namespace mq

@@ -287,7 +287,8 @@ DecPlan tcdec_plan(const WeightView &w, int device, int max_grid) {
 }
 
 int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const float *bias, float *y, int64_t ldy,
-                 cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort, const float *gate) {
+                 cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort, const float *gate,
+                 const float *resid) {
   const int bn = dec_tile_rows(mm);
   MQ_CUDA(launch_pdl(dec_prep_kernel, dim3(plan.steps, (bn + 7) / 8), dim3(256), 0, s, x, ldx, mm, w.cols, plan.kpad,
                      bn, buf.x2, buf.xsum, buf.xinv, (int)(w.qtype == MQ_Q4_1)));
@@ -297,7 +298,7 @@ int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const
   if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf.x2, 2 * bn, plan.kpad, plan.kpad, 64, 2 * bn)))
     return rc;
   DecArgs a{w, mm, buf.xinv, buf.xsum, bias, y, ldy, buf.partial, buf.tickets, plan.steps, plan.tiles, buf.err,
-            nan_on_abort, gate};
+            nan_on_abort, gate, resid};
   cudaError_t e;
   switch (w.qtype) {
   case MQ_Q8_0: e = launch_tcdec_q<MQ_Q8_0>(tx, a, plan.grid, mm, s); break;
@@ -310,7 +311,7 @@ int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const
 
 // tcgen05 decode GEMM: up to 32 activation rows per launch (split + kernel).
 int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-              cudaStream_t s, const float *gate) {
+              cudaStream_t s, const float *gate, const float *resid) {
   int *err_dev = nullptr, *err_host = nullptr;
   int rc = err_flag(wt->device, &err_dev, &err_host);
   if (rc) return rc;
@@ -340,7 +341,7 @@ int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
     buf.tickets = tickets;
     buf.err = err_dev;
     if ((rc = tcdec_launch(w, x + (int64_t)i0 * ldx, mm, ldx, bias, y + (int64_t)i0 * ldy, ldy, s, plan, buf, 0,
-                           gate ? gate + (int64_t)i0 * ldy : nullptr)))
+                           gate ? gate + (int64_t)i0 * ldy : nullptr, resid ? resid + (int64_t)i0 * ldy : nullptr)))
       return rc;
   }
   return MQ_OK;
@@ -381,7 +382,7 @@ int sdec_max_m() {
 // are read by TMA straight from x when its base and row stride are 16-byte
 // aligned; otherwise they are first copied to an aligned scratch.
 int run_sdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-             cudaStream_t s, const float *gate) {
+             cudaStream_t s, const float *gate, const float *resid) {
   int *err_dev = nullptr, *err_host = nullptr;
   int rc = err_flag(wt->device, &err_dev, &err_host);
   if (rc) return rc;
@@ -421,7 +422,8 @@ int run_sdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const floa
                         CU_TENSOR_MAP_SWIZZLE_NONE)))
       return rc;
     SdecArgs a{w, mm, bias, y + (int64_t)i0 * ldy, ldy, reinterpret_cast<float *>(base), tickets, plan.steps,
-               plan.tiles, err_dev, 0, gate ? gate + (int64_t)i0 * ldy : nullptr};
+               plan.tiles, err_dev, 0, gate ? gate + (int64_t)i0 * ldy : nullptr,
+               resid ? resid + (int64_t)i0 * ldy : nullptr};
     cudaError_t e;
     switch (w.qtype) {
     case MQ_Q8_0: e = launch_sdec_q<MQ_Q8_0>(tx, a, plan.grid, mc, s); break;
@@ -467,7 +469,7 @@ int i8dec_max_m() {
 
 // int8 tensor-core decode: up to 4 activation rows per launch.
 int run_i8dec(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-              cudaStream_t s, const float *gate = nullptr) {
+              cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr) {
   int *err_dev = nullptr, *err_host = nullptr;
   int rc = err_flag(wt->device, &err_dev, &err_host);
   if (rc) return rc;
@@ -486,7 +488,8 @@ int run_i8dec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
     void *ws = nullptr;
     if ((rc = workspace_for(wt->device, s, pbytes + 1024, &ws))) return rc;
     I8Args a{w, mm, x + (int64_t)i0 * ldx, ldx, bias, y + (int64_t)i0 * ldy, ldy, static_cast<float *>(ws), tickets,
-             plan.steps, plan.tiles, err_dev, 0, gate ? gate + (int64_t)i0 * ldy : nullptr};
+             plan.steps, plan.tiles, err_dev, 0, gate ? gate + (int64_t)i0 * ldy : nullptr,
+             resid ? resid + (int64_t)i0 * ldy : nullptr};
     cudaError_t e;
     switch (w.qtype) {
     case MQ_Q8_0: e = launch_i8dec_q<MQ_Q8_0>(a, plan.grid, mc, s); break;
@@ -499,7 +502,7 @@ int run_i8dec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
 }
 
 int run_gemm(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-             cudaStream_t s, const float *gate) {
+             cudaStream_t s, const float *gate, const float *resid) {
   int *err_dev = nullptr, *err_host = nullptr;
   int rc = err_flag(wt->device, &err_dev, &err_host);
   if (rc) return rc;
@@ -524,7 +527,7 @@ int run_gemm(const mq_weight *wt, const float *x, int m, int64_t ldx, const floa
   CUtensorMap th, tl;
   if ((rc = make_tmap_bf16(&th, xh, m, kpad, BN))) return rc;
   if ((rc = make_tmap_bf16(&tl, xl, m, kpad, BN))) return rc;
-  GemmArgs a{w, y, ldy, bias, m, (w.nb + 1) / 2, err_dev, gate};
+  GemmArgs a{w, y, ldy, bias, m, (w.nb + 1) / 2, err_dev, gate, resid};
   cudaError_t e;
   switch (w.qtype) {
   case MQ_Q8_0: e = launch_gemm_t<MQ_Q8_0, BN, STAGES>(th, tl, a, s); break;

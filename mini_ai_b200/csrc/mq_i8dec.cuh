@@ -110,7 +110,8 @@ struct I8Args {
   int tiles;
   int *err;
   int nan_on_abort;
-  const float *gate = nullptr;  // fused gate/up product: y = silu(gate) * (product + bias); gate [m, ldy]
+  const float *gate = nullptr;   // fused gate/up product: y = silu(gate) * (product + bias); gate [m, ldy]
+  const float *resid = nullptr;  // residual add: y = resid + (product + bias); resid [m, ldy], may be y
 };
 
 template <int QT, int MC>
@@ -556,7 +557,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
           const float bias = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
           for (int c = 0; c < MC; ++c)
-            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = swiglu_out(acc[c] + bias, a.gate, (int64_t)c * a.ldy + n);
+            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = epilogue_out(acc[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n);
         }
         return;
       }
@@ -584,7 +585,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
           const float bias = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
           for (int c = 0; c < MC; ++c)
-            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = swiglu_out(tot[c] + bias, a.gate, (int64_t)c * a.ldy + n);
+            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = epilogue_out(tot[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n);
         }
         if (warp == 16 && lane == 0) a.tickets[tile] = 0;  // ready for the next launch
       }

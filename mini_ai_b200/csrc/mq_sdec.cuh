@@ -73,7 +73,8 @@ struct SdecArgs {
   int tiles;
   int *err;
   int nan_on_abort;
-  const float *gate = nullptr;  // fused gate/up product: y = silu(gate) * (product + bias); gate [m, ldy]
+  const float *gate = nullptr;   // fused gate/up product: y = silu(gate) * (product + bias); gate [m, ldy]
+  const float *resid = nullptr;  // residual add: y = resid + (product + bias); resid [m, ldy], may be y
 };
 
 template <int QT, int MC>
@@ -186,7 +187,7 @@ __global__ void __launch_bounds__(kSdThreads, SdCfg<QT, MC>::kCtasPerSm)
             const float bias = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
             for (int i = 0; i < MC; ++i)
-              if (i < a.m) a.y[(int64_t)i * a.ldy + n] = swiglu_out(tot[i] + bias, a.gate, (int64_t)i * a.ldy + n);
+              if (i < a.m) a.y[(int64_t)i * a.ldy + n] = epilogue_out(tot[i] + bias, a.gate, a.resid, (int64_t)i * a.ldy + n);
           }
         } else {
           const int kind = (tile == g0 / S) ? 0 : 1;
@@ -213,7 +214,7 @@ __global__ void __launch_bounds__(kSdThreads, SdCfg<QT, MC>::kCtasPerSm)
               const float bias = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
               for (int i = 0; i < MC; ++i)
-                if (i < a.m) a.y[(int64_t)i * a.ldy + n] = swiglu_out(sum[i] + bias, a.gate, (int64_t)i * a.ldy + n);
+                if (i < a.m) a.y[(int64_t)i * a.ldy + n] = epilogue_out(sum[i] + bias, a.gate, a.resid, (int64_t)i * a.ldy + n);
             }
             if (r == 0) a.tickets[tile] = 0;  // ready for the next launch
           }

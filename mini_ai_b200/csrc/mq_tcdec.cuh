@@ -101,7 +101,8 @@ struct DecArgs {
   int tiles;
   int *err;
   int nan_on_abort;      // on a timed-out wait, write NaN outputs instead of skipping them
-  const float *gate = nullptr;  // fused gate/up product: y = silu(gate) * (product + bias); gate [m, ldy]
+  const float *gate = nullptr;   // fused gate/up product: y = silu(gate) * (product + bias); gate [m, ldy]
+  const float *resid = nullptr;  // residual add: y = resid + (product + bias); resid [m, ldy], may be y
 };
 
 template <int QT, int BN>
@@ -477,7 +478,7 @@ __global__ void __launch_bounds__(DecCfg<QT, BN>::kThreads, 1)
           const float bias = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
           for (int c = 0; c < NC; ++c)
-            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = swiglu_out(acc[c] + bias, a.gate, (int64_t)c * a.ldy + n);
+            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = epilogue_out(acc[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n);
         }
         return;
       }
@@ -509,7 +510,7 @@ __global__ void __launch_bounds__(DecCfg<QT, BN>::kThreads, 1)
           const float bias = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
           for (int c = 0; c < NC; ++c)
-            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = swiglu_out(tot[c] + bias, a.gate, (int64_t)c * a.ldy + n);
+            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = epilogue_out(tot[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n);
         }
         if (warp == 12 && lane == 0) a.tickets[tile] = 0;  // ready for the next launch
       }

@@ -37,7 +37,7 @@ inline int dec_tile_rows(int m) { return m <= 8 ? 8 : (m <= 16 ? 16 : 32); }
 // of leaving them unwritten.
 int tcdec_launch(const WeightView &w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
                  cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort,
-                 const float *gate = nullptr);
+                 const float *gate = nullptr, const float *resid = nullptr);
 
 bool gemm_supported(int device);
 

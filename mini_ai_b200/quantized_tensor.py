@@ -199,6 +199,33 @@ class CudaWeight:
                               out2.data_ptr(), out2.stride(0), _stream_handle(stream)), "LinearDispatch")
         return out2.view(self.rows) if squeeze and out.dim() != 1 else out
 
+    def linear_residual(self, x, residual, bias=None, out=None, stream=None):
+        """residual + (x · Wᵀ + bias), the linear and ForwardCuda's residual AddKernel
+        (src/cuda_backend.cu:236-240) in one launch; ``out`` may be ``residual`` (in place)."""
+        torch = _torch()
+        if x.dtype != torch.float32 or not x.is_cuda:
+            raise RuntimeError("Linear requires F32 activations on the weight's device")
+        x2 = x.unsqueeze(0) if x.dim() == 1 else x
+        if x2.dim() != 2 or x2.shape[1] != self.cols:
+            raise RuntimeError("LinearDispatch: dimension mismatch")
+        if x2.stride(1) != 1:
+            x2 = x2.contiguous()
+        m = x2.shape[0]
+        r2 = residual.view(1, -1) if residual.dim() == 1 else residual
+        if tuple(r2.shape) != (m, self.rows) or r2.dtype != torch.float32 or r2.stride(1) != 1:
+            raise RuntimeError("ElementwiseAdd: shape mismatch")
+        if out is None:
+            out = torch.empty_like(r2)
+        o2 = out.view(1, -1) if out.dim() == 1 else out
+        if o2.shape != r2.shape or o2.stride(0) != r2.stride(0):
+            raise RuntimeError("output shape mismatch (the output must have the residual's layout)")
+        if bias is not None and (bias.numel() != self.rows or bias.dtype != torch.float32):
+            raise RuntimeError("bias shape mismatch")
+        check(lib().mq_linear_residual(self.handle, x2.data_ptr(), m, x2.stride(0),
+                                       bias.data_ptr() if bias is not None else None, r2.data_ptr(), o2.data_ptr(),
+                                       o2.stride(0), _stream_handle(stream)), "LinearDispatch")
+        return out
+
     def close(self) -> None:
         if getattr(self, "handle", None):
             lib().mq_weight_destroy(self.handle)

@@ -298,3 +298,34 @@ def test_swiglu_validation(mq, cuda_device):
         mq.LinearSwiGlu(dev(np.zeros((1, 64), np.float32), cuda_device), wa, wa)
     wa.close()
     wb.close()
+
+
+@pytest.mark.parametrize("path", [0] + sorted(PATHS), ids=lambda p: PATHS.get(p, "automatic"))
+@pytest.mark.parametrize("q", QTYPES, ids=lambda q: NAMES[q])
+def test_residual_add_against_oracle(mq, oracle, cuda_device, path, q):
+    """mq_linear_residual = residual + (x · Wᵀ + bias) (the wo / w_down linear and ForwardCuda's
+    AddKernel, src/cuda_backend.cu:236-240), in place and out of place, through every kernel:
+    within the parity bound of the oracle, and bit-identical to the unfused product plus the add."""
+    torch = _torch()
+    ms = {0: [1, 3, 16, 40], 1: [1, 3, 5], 3: [1, 2, 4, 5], 4: [1, 5, 16, 33], 2: [1, 129]}[path]
+    for rows, cols in [(300, 4097), (1024, 4096)]:
+        for m in ms:
+            s, x, y_ref, bound = _llama_case(mq, oracle, q, rows, cols, m, seed=rows * 17 + m + path * 7)
+            rng = np.random.default_rng(rows + m)
+            r = rng.standard_normal((m, rows)).astype(np.float32)
+            b = (rng.standard_normal(rows) * 0.1).astype(np.float32)
+            ref = r.astype(np.float64) + (y_ref.astype(np.float64) + b.astype(np.float64))
+            w = mq.CudaWeight(s, device=cuda_device)
+            prev = mq.set_path(path)
+            try:
+                xd, rd, bd = dev(x, cuda_device), dev(r, cuda_device), dev(b, cuda_device)
+                y = w.linear_residual(xd, rd, bias=bd)
+                unfused = rd + w.linear(xd, bias=bd)
+                inplace = rd.clone()
+                w.linear_residual(xd, inplace, bias=bd, out=inplace)
+                torch.cuda.synchronize(cuda_device)
+            finally:
+                mq.set_path(prev)
+            assert_linear_close(y.cpu().numpy(), ref, bound)
+            assert torch.equal(y, unfused) and torch.equal(inplace, y)
+            w.close()
