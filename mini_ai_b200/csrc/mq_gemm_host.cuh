@@ -189,26 +189,32 @@ int make_tmap(CUtensorMap *map, CUtensorMapDataType dtype, int elem, const void 
   return MQ_OK;
 }
 
-template <int QT, int BN, int NC>
+template <int QT, int BN, int NC, bool EPI>
 cudaError_t launch_tcdec_t(const CUtensorMap &tx, const DecArgs &a, int grid, cudaStream_t s) {
   using L = DecCfg<QT, BN>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(tcdec_kernel<QT, BN, NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    cudaError_t e = cudaFuncSetAttribute(tcdec_kernel<QT, BN, NC, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  const cudaError_t e = launch_pdl(tcdec_kernel<QT, BN, NC>, dim3(grid), dim3(L::kThreads), L::kAlloc, s, tx, a);
+  const cudaError_t e = launch_pdl(tcdec_kernel<QT, BN, NC, EPI>, dim3(grid), dim3(L::kThreads), L::kAlloc, s, tx, a);
   count_launch();
   return e;
 }
 
 template <int QT>
 cudaError_t launch_tcdec_q(const CUtensorMap &tx, const DecArgs &a, int grid, int m, cudaStream_t s) {
-  if (m <= 4) return launch_tcdec_t<QT, 8, 4>(tx, a, grid, s);
-  if (m <= 8) return launch_tcdec_t<QT, 8, 8>(tx, a, grid, s);
-  if (m <= 16) return launch_tcdec_t<QT, 16, 16>(tx, a, grid, s);
-  return launch_tcdec_t<QT, 32, 32>(tx, a, grid, s);
+  if (a.gate || a.resid) {
+    if (m <= 4) return launch_tcdec_t<QT, 8, 4, true>(tx, a, grid, s);
+    if (m <= 8) return launch_tcdec_t<QT, 8, 8, true>(tx, a, grid, s);
+    if (m <= 16) return launch_tcdec_t<QT, 16, 16, true>(tx, a, grid, s);
+    return launch_tcdec_t<QT, 32, 32, true>(tx, a, grid, s);
+  }
+  if (m <= 4) return launch_tcdec_t<QT, 8, 4, false>(tx, a, grid, s);
+  if (m <= 8) return launch_tcdec_t<QT, 8, 8, false>(tx, a, grid, s);
+  if (m <= 16) return launch_tcdec_t<QT, 16, 16, false>(tx, a, grid, s);
+  return launch_tcdec_t<QT, 32, 32, false>(tx, a, grid, s);
 }
 
 template <int QT, int BN, int STAGES>
@@ -437,25 +443,30 @@ int run_sdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const floa
 
 namespace {
 
-template <int QT, int MC>
+template <int QT, int MC, bool EPI>
 cudaError_t launch_i8dec_t(const I8Args &a, int grid, cudaStream_t s) {
   using L = I8Cfg<QT, MC>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(i8dec_kernel<QT, MC>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    cudaError_t e = cudaFuncSetAttribute(i8dec_kernel<QT, MC, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  const cudaError_t e = launch_pdl(i8dec_kernel<QT, MC>, dim3(grid), dim3(kI8Threads), L::kAlloc, s, a);
+  const cudaError_t e = launch_pdl(i8dec_kernel<QT, MC, EPI>, dim3(grid), dim3(kI8Threads), L::kAlloc, s, a);
   count_launch();
   return e;
 }
 
 template <int QT>
 cudaError_t launch_i8dec_q(const I8Args &a, int grid, int mc, cudaStream_t s) {
-  if (mc == 1) return launch_i8dec_t<QT, 1>(a, grid, s);
-  if (mc == 2) return launch_i8dec_t<QT, 2>(a, grid, s);
-  return launch_i8dec_t<QT, 4>(a, grid, s);
+  if (a.gate || a.resid) {
+    if (mc == 1) return launch_i8dec_t<QT, 1, true>(a, grid, s);
+    if (mc == 2) return launch_i8dec_t<QT, 2, true>(a, grid, s);
+    return launch_i8dec_t<QT, 4, true>(a, grid, s);
+  }
+  if (mc == 1) return launch_i8dec_t<QT, 1, false>(a, grid, s);
+  if (mc == 2) return launch_i8dec_t<QT, 2, false>(a, grid, s);
+  return launch_i8dec_t<QT, 4, false>(a, grid, s);
 }
 
 }  // namespace

@@ -225,7 +225,9 @@ __host__ __device__ inline int i8_slot_elem(int qtype, int c, int p) {
   return 2 * t + (qtype == MQ_Q8_0 ? q8[p] : q4[p]) + 16 * h;
 }
 
-template <int QT, int MC>
+// EPI: the output write applies the epilogues of I8Args::gate / resid (a separate
+// instantiation: the plain product is compiled without them).
+template <int QT, int MC, bool EPI>
 __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
   using L = I8Cfg<QT, MC>;
   constexpr int PS = L::PS, NB = L::NB, DS = L::DS, NA = L::NA, ND = L::ND, NCOL = L::NCOL, BB = L::BB;
@@ -557,7 +559,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
           const float bias = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
           for (int c = 0; c < MC; ++c)
-            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = epilogue_out(acc[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n);
+            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = EPI ? epilogue_out(acc[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n) : acc[c] + bias;
         }
         return;
       }
@@ -585,7 +587,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
           const float bias = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
           for (int c = 0; c < MC; ++c)
-            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = epilogue_out(tot[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n);
+            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = EPI ? epilogue_out(tot[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n) : tot[c] + bias;
         }
         if (warp == 16 && lane == 0) a.tickets[tile] = 0;  // ready for the next launch
       }

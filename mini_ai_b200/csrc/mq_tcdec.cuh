@@ -229,7 +229,9 @@ __device__ __forceinline__ void tmem_ld_n(uint32_t taddr, uint32_t (&r)[N]) {
   }
 }
 
-template <int QT, int BN, int NC>
+// EPI: the output write applies the epilogues of DecArgs::gate / resid (a
+// separate instantiation: the plain product is compiled without them).
+template <int QT, int BN, int NC, bool EPI>
 __global__ void __launch_bounds__(DecCfg<QT, BN>::kThreads, 1)
     tcdec_kernel(const __grid_constant__ CUtensorMap tm_x, const DecArgs a) {
   using L = DecCfg<QT, BN>;
@@ -478,7 +480,7 @@ __global__ void __launch_bounds__(DecCfg<QT, BN>::kThreads, 1)
           const float bias = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
           for (int c = 0; c < NC; ++c)
-            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = epilogue_out(acc[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n);
+            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = EPI ? epilogue_out(acc[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n) : acc[c] + bias;
         }
         return;
       }
@@ -510,7 +512,7 @@ __global__ void __launch_bounds__(DecCfg<QT, BN>::kThreads, 1)
           const float bias = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
           for (int c = 0; c < NC; ++c)
-            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = epilogue_out(tot[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n);
+            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = EPI ? epilogue_out(tot[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n) : tot[c] + bias;
         }
         if (warp == 12 && lane == 0) a.tickets[tile] = 0;  // ready for the next launch
       }
