@@ -195,8 +195,12 @@ void mq_comm_destroy(mq_comm *c);
  * [m, ldy] with ldy >= N. Stream-ordered on `stream`; every rank must call it
  * with the same m, in the same order relative to its other collectives. The
  * peer-memory gather (see mq_comm_create) takes outputs with m * R <= 2^20 and
- * may be captured in a CUDA graph; a peer that does not arrive within 1 s
- * makes the next call on this device fail with MQ_ERR_TIMEOUT. */
+ * may be captured in a CUDA graph. A peer that does not arrive within the wait
+ * limit (MQ_P2P_WAIT_NS nanoseconds in the environment at mq_comm_create,
+ * default 1 s) leaves NaN in that peer's output columns and poisons the
+ * communicator: its next call and every later peer-memory gather on it fail
+ * with MQ_ERR_TIMEOUT (replays of a captured graph write NaN without
+ * waiting); destroy it and create a new one. */
 int mq_linear_sharded_allgather(const mq_weight *shard, const float *x, int m, int ldx, const float *bias,
                                 float *y, int ldy, mq_comm *comm, void *stream);
 

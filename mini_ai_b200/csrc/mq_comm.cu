@@ -21,7 +21,12 @@
 // with it the half) lives in device memory and is advanced by the pull
 // kernel, so a CUDA graph that captured these launches replays correctly.
 // A rank can be at most one call ahead of a peer (its next push waits for the
-// peer's flags of the current call), so two halves are enough. Outputs larger
+// peer's flags of the current call), so two halves are enough. A peer that
+// does not arrive within the wait limit (MQ_P2P_WAIT_NS, default 1 s) poisons
+// the communicator: the pull writes NaN into the missing columns, raises the
+// communicator's error flag, and from then on every peer-memory gather of
+// this communicator fails with MQ_ERR_TIMEOUT at once (replays of a captured
+// graph write NaN without waiting); the epoch no longer matters. Outputs larger
 // than a slot, communicators whose ranks could not all map each other's
 // regions, and processes without MQ_P2P_GATHER=1 use NCCL's all-gather.
 //
@@ -42,12 +47,11 @@
 
 namespace mq {
 int gather_workspace_for(int device, cudaStream_t s, size_t bytes, void **out);
-int device_err_flag(int device, int **dev_ptr, int **host_ptr);
 void count_launch(int n);
 
 constexpr int kP2PMaxRanks = 8;
 constexpr size_t kP2PSlotFloats = size_t(1) << 20;  // 4 MiB per slot: m * rows_per_rank <= 1,048,576
-constexpr uint64_t kP2PWaitNs = 1000000000ull;
+constexpr uint64_t kP2PWaitNs = 1000000000ull;  // default wait limit for a peer's arrival flag
 }  // namespace mq
 
 struct mq_comm {
@@ -56,6 +60,9 @@ struct mq_comm {
   bool p2p = false;                           // peer-memory gather set up on every rank
   char *stage = nullptr;                      // this rank's staging region
   char *peer[mq::kP2PMaxRanks] = {nullptr};   // every rank's region as mapped here (own at [rank])
+  uint64_t wait_ns = mq::kP2PWaitNs;           // bound of the pull kernel's wait for a peer
+  int *err_host = nullptr, *err_dev = nullptr;  // mapped flag: a peer gather of this communicator timed out
+  bool poisoned = false;                       // a timeout was reported: peer gathers fail from then on
 };
 
 namespace mq {
@@ -109,7 +116,7 @@ __global__ void interleave_kernel(const float *__restrict__ g, int nranks, int m
 }
 
 // Byte layout of a staging region: data [2][G][slot], flags [2][G] u32,
-// counters {epoch, push arrivals, pull arrivals} u32.
+// counters {epoch, push arrivals, pull arrivals, poisoned} u32.
 __host__ __device__ inline size_t p2p_data_bytes(int G) { return 2 * (size_t)G * kP2PSlotFloats * sizeof(float); }
 __host__ __device__ inline size_t p2p_region_bytes(int G) { return p2p_data_bytes(G) + (2 * (size_t)G + 4) * 4; }
 
@@ -118,7 +125,8 @@ struct P2PArgs {
   int64_t ldy;
   int m, R, G, rank;
   char *base[kP2PMaxRanks];
-  int *err;
+  int *err;          // the communicator's host-mapped timeout flag
+  uint64_t wait_ns;  // bound of the wait for a peer's flag
 };
 
 __device__ __forceinline__ uint32_t *p2p_flags(char *base, int G) {
@@ -171,7 +179,9 @@ __global__ void __launch_bounds__(256) p2p_push_kernel(const P2PArgs a) {
 }
 
 // Waits for every peer's slice of this epoch, then copies the peers' slots
-// into their columns of the output; the last CTA advances the epoch.
+// into their columns of the output; the last CTA advances the epoch. A wait
+// that runs out (or a communicator poisoned by an earlier one) writes NaN
+// into the peers' columns instead and raises the error flag.
 template <bool VEC>
 __global__ void __launch_bounds__(256) p2p_pull_kernel(const P2PArgs a) {
   __shared__ int s_ok;
@@ -181,23 +191,36 @@ __global__ void __launch_bounds__(256) p2p_pull_kernel(const P2PArgs a) {
   const uint32_t e = *reinterpret_cast<volatile uint32_t *>(&ctl[0]) + 1u;
   const int half = (int)(e & 1u);
   if (threadIdx.x == 0) {
-    int ok = 1;
+    int ok = *reinterpret_cast<volatile uint32_t *>(&ctl[3]) == 0u;
     const uint64_t t0 = sm100::globaltimer_ns();
     for (int p = 0; p < a.G && ok; ++p) {
       if (p == a.rank) continue;
       for (uint32_t it = 0; ld_acquire_sys(flags + half * a.G + p) != e; ++it) {
-        if ((it & 63u) == 63u && sm100::globaltimer_ns() - t0 > kP2PWaitNs) {
+        if ((it & 63u) == 63u && (sm100::globaltimer_ns() - t0 > a.wait_ns ||
+                                  *reinterpret_cast<volatile uint32_t *>(&ctl[3]) != 0u)) {
           ok = 0;
-          atomicExch(a.err, 1);
           break;
         }
       }
+    }
+    if (!ok) {
+      atomicExch(reinterpret_cast<unsigned int *>(&ctl[3]), 1u);
+      atomicExch(a.err, 1);
     }
     __threadfence();
     s_ok = ok;
   }
   __syncthreads();
-  if (s_ok) {
+  if (!s_ok) {
+    const int64_t n = (int64_t)a.m * a.R;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int p = 0; p < a.G; ++p) {
+      if (p == a.rank) continue;
+      float *dst = a.y + (int64_t)p * a.R;
+      for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        dst[(i / a.R) * a.ldy + i % a.R] = __int_as_float(0x7fc00000);
+    }
+  } else {
     const int64_t n = (int64_t)a.m * a.R;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int p = 0; p < a.G; ++p) {
@@ -227,36 +250,64 @@ __global__ void __launch_bounds__(256) p2p_pull_kernel(const P2PArgs a) {
   }
 }
 
-// Maps every rank's staging region on every rank; false (and nothing held)
-// unless all ranks succeeded.
-bool p2p_setup(mq_comm *c) {
-  const int G = c->nranks;
+// Device buffers and stream of the set-up exchanges, allocated before the
+// rank joins the NCCL communicator, so that every rank that reaches an
+// exchange has valid buffers (a rank that could not allocate them fails
+// mq_comm_create before joining instead of leaving its peers waiting in a
+// collective it cannot take part in).
+struct P2PExchange {
+  void *buf = nullptr;  // [G] records, then [G] agreement flags
+  cudaStream_t s = nullptr;
+  void release() {
+    if (s) cudaStreamDestroy(s);
+    if (buf) cudaFree(buf);
+    s = nullptr;
+    buf = nullptr;
+  }
+};
+
+struct P2PRec {
+  int ok;
+  int pad[3];
+  cudaIpcMemHandle_t h;
+};
+
+bool p2p_wanted(int G) {
   if (G < 2 || G > kP2PMaxRanks) return false;
   const char *env = std::getenv("MQ_P2P_GATHER");  // opt-in: MQ_P2P_GATHER=1
-  if (!env || env[0] != '1') return false;
+  return env && env[0] == '1';
+}
+
+cudaError_t p2p_exchange_alloc(int G, P2PExchange *x) {
+  cudaError_t e = cudaMalloc(&x->buf, (sizeof(P2PRec) + sizeof(int)) * G);
+  if (e == cudaSuccess) e = cudaStreamCreate(&x->s);
+  if (e != cudaSuccess) x->release();
+  return e;
+}
+
+// Maps every rank's staging region on every rank; false (and nothing held)
+// unless all ranks succeeded. `x` holds the exchange buffers (allocated before
+// the communicator was joined).
+bool p2p_setup(mq_comm *c, P2PExchange &x) {
+  const int G = c->nranks;
   const size_t bytes = p2p_region_bytes(G);
   bool ok = cudaMalloc(&c->stage, bytes) == cudaSuccess;
   ok = ok && cudaMemset(c->stage, 0, bytes) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+  ok = ok && cudaHostAlloc(&c->err_host, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable) == cudaSuccess;
+  if (ok) {
+    *c->err_host = 0;
+    ok = cudaHostGetDevicePointer(&c->err_dev, c->err_host, 0) == cudaSuccess;
+  }
   // Exchange {ok, handle} records over NCCL (in place: every rank sends its own record).
-  struct Rec {
-    int ok;
-    int pad[3];
-    cudaIpcMemHandle_t h;
-  };
-  Rec mine{};
+  P2PRec mine{};
   mine.ok = ok && cudaIpcGetMemHandle(&mine.h, c->stage) == cudaSuccess;
-  Rec *d_recs = nullptr;
-  Rec recs[kP2PMaxRanks];
-  cudaStream_t s = nullptr;
-  bool ex = cudaMalloc(&d_recs, sizeof(Rec) * G) == cudaSuccess && cudaStreamCreate(&s) == cudaSuccess &&
-            cudaMemcpy(d_recs + c->rank, &mine, sizeof(Rec), cudaMemcpyHostToDevice) == cudaSuccess;
+  P2PRec *d_recs = static_cast<P2PRec *>(x.buf);
+  P2PRec recs[kP2PMaxRanks];
+  bool ex = cudaMemcpy(d_recs + c->rank, &mine, sizeof(P2PRec), cudaMemcpyHostToDevice) == cudaSuccess;
   // Every rank takes part in the exchange, whatever its own state, so that no rank waits alone.
-  const ncclResult_t nr = nccl().all_gather(d_recs ? (const void *)(d_recs + c->rank) : nullptr, d_recs, sizeof(Rec),
-                                            ncclUint8, c->comm, s);
-  ex = ex && nr == ncclSuccess && cudaStreamSynchronize(s) == cudaSuccess &&
-       cudaMemcpy(recs, d_recs, sizeof(Rec) * G, cudaMemcpyDeviceToHost) == cudaSuccess;
-  if (s) cudaStreamDestroy(s);
-  if (d_recs) cudaFree(d_recs);
+  const ncclResult_t nr = nccl().all_gather(d_recs + c->rank, d_recs, sizeof(P2PRec), ncclUint8, c->comm, x.s);
+  ex = ex && nr == ncclSuccess && cudaStreamSynchronize(x.s) == cudaSuccess &&
+       cudaMemcpy(recs, d_recs, sizeof(P2PRec) * G, cudaMemcpyDeviceToHost) == cudaSuccess;
   bool all = ex;
   for (int p = 0; all && p < G; ++p) all = recs[p].ok != 0;
   if (all) {
@@ -274,18 +325,13 @@ bool p2p_setup(mq_comm *c) {
     }
   }
   // Agree that every rank mapped every peer (a second exchange of one flag each).
-  int *d_ok = nullptr;
+  int *d_ok = reinterpret_cast<int *>(static_cast<char *>(x.buf) + sizeof(P2PRec) * G);
   int oks[kP2PMaxRanks] = {0};
   const int my_ok = all ? 1 : 0;
-  cudaStream_t s2 = nullptr;
-  bool ex2 = cudaMalloc(&d_ok, sizeof(int) * G) == cudaSuccess && cudaStreamCreate(&s2) == cudaSuccess &&
-             cudaMemcpy(d_ok + c->rank, &my_ok, sizeof(int), cudaMemcpyHostToDevice) == cudaSuccess;
-  const ncclResult_t nr2 =
-      nccl().all_gather(d_ok ? (const void *)(d_ok + c->rank) : nullptr, d_ok, 1, ncclInt32, c->comm, s2);
-  ex2 = ex2 && nr2 == ncclSuccess && cudaStreamSynchronize(s2) == cudaSuccess &&
+  bool ex2 = cudaMemcpy(d_ok + c->rank, &my_ok, sizeof(int), cudaMemcpyHostToDevice) == cudaSuccess;
+  const ncclResult_t nr2 = nccl().all_gather(d_ok + c->rank, d_ok, 1, ncclInt32, c->comm, x.s);
+  ex2 = ex2 && nr2 == ncclSuccess && cudaStreamSynchronize(x.s) == cudaSuccess &&
         cudaMemcpy(oks, d_ok, sizeof(int) * G, cudaMemcpyDeviceToHost) == cudaSuccess;
-  if (s2) cudaStreamDestroy(s2);
-  if (d_ok) cudaFree(d_ok);
   bool agreed = ex2;
   for (int p = 0; agreed && p < G; ++p) agreed = oks[p] != 0;
   if (!agreed) {
@@ -294,8 +340,15 @@ bool p2p_setup(mq_comm *c) {
     for (int p = 0; p < G; ++p) c->peer[p] = nullptr;
     if (c->stage) cudaFree(c->stage);
     c->stage = nullptr;
+    if (c->err_host) cudaFreeHost(c->err_host);
+    c->err_host = c->err_dev = nullptr;
     cudaGetLastError();  // the fallback is NCCL: clear a failed call's error state
     return false;
+  }
+  const char *w = std::getenv("MQ_P2P_WAIT_NS");
+  if (w && *w) {
+    const long long v = std::atoll(w);
+    if (v > 0) c->wait_ns = (uint64_t)v;
   }
   return true;
 }
@@ -305,6 +358,8 @@ void p2p_release(mq_comm *c) {
   for (int p = 0; p < c->nranks; ++p)
     if (p != c->rank && c->peer[p]) cudaIpcCloseMemHandle(c->peer[p]);
   if (c->stage) cudaFree(c->stage);
+  if (c->err_host) cudaFreeHost(c->err_host);
+  c->err_host = c->err_dev = nullptr;
   c->p2p = false;
 }
 
@@ -358,25 +413,35 @@ int mq_comm_create(int device, int nranks, int rank, const void *id, size_t len,
   int prev = -1;
   if ((e = cudaGetDevice(&prev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if ((e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  P2PExchange xch;
+  const bool want_p2p = p2p_wanted(nranks);
+  if (want_p2p && (e = p2p_exchange_alloc(nranks, &xch)) != cudaSuccess) {
+    cudaSetDevice(prev);
+    return cuda_fail(e, "peer-gather exchange buffers (before joining the communicator)");
+  }
   ncclUniqueId u;
   memcpy(u.internal, id, NCCL_UNIQUE_ID_BYTES);
   ncclComm_t comm = nullptr;
   const ncclResult_t r = nccl().comm_init_rank(&comm, nranks, u, rank);
-  cudaSetDevice(prev);
-  if (r != ncclSuccess) return nccl_fail(r, "ncclCommInitRank");
+  if (r != ncclSuccess) {
+    xch.release();
+    cudaSetDevice(prev);
+    return nccl_fail(r, "ncclCommInitRank");
+  }
   auto *c = new (std::nothrow) mq_comm;
   if (!c) {
+    xch.release();
     nccl().comm_destroy(comm);
+    cudaSetDevice(prev);
     return fail(MQ_ERR_INVALID, "out of host memory");
   }
   c->device = device;
   c->nranks = nranks;
   c->rank = rank;
   c->comm = comm;
-  if ((e = cudaSetDevice(device)) == cudaSuccess) {
-    c->p2p = p2p_setup(c);
-    cudaSetDevice(prev);
-  }
+  if (want_p2p) c->p2p = p2p_setup(c, xch);
+  xch.release();
+  cudaSetDevice(prev);
   *out = c;
   return MQ_OK;
 }
@@ -420,11 +485,15 @@ int mq_linear_sharded_allgather(const mq_weight *w, const float *x, int m, int l
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const float *bias_slice = bias ? bias + (int64_t)r * R : nullptr;
   if (comm->p2p && (size_t)m * R <= kP2PSlotFloats) {  // peer-memory gather
-    int *err_dev = nullptr, *err_host = nullptr;
-    int rc = device_err_flag(w->device, &err_dev, &err_host);
+    if (*(volatile int *)comm->err_host) comm->poisoned = true;
+    if (comm->poisoned)
+      return fail(MQ_ERR_TIMEOUT,
+                  "peer-memory gather: a peer did not arrive within %llu ns in an earlier call on rank %d; this "
+                  "communicator's gathers are disabled (destroy it and create a new one)",
+                  (unsigned long long)comm->wait_ns, r);
+    int rc = mq_linear(w, x, m, ldx, bias_slice, y + (int64_t)r * R, ldy, stream);
     if (rc) return rc;
-    if ((rc = mq_linear(w, x, m, ldx, bias_slice, y + (int64_t)r * R, ldy, stream))) return rc;
-    P2PArgs a{y, (int64_t)ldy, m, R, G, r, {}, err_dev};
+    P2PArgs a{y, (int64_t)ldy, m, R, G, r, {}, comm->err_dev, comm->wait_ns};
     for (int p = 0; p < G; ++p) a.base[p] = comm->peer[p];
     const bool vec = R % 4 == 0 && ldy % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
     const int64_t n = (int64_t)m * R / (vec ? 4 : 1);

@@ -4,6 +4,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -16,6 +17,23 @@
 namespace mq {
 
 namespace {
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) acts on the calling
+// thread's current device only, so each launcher keeps one bit per device
+// (set once the attribute is in place there). Two host threads may both set
+// it on first use; that is harmless, and the mask itself is atomic.
+template <typename Kernel>
+cudaError_t raise_smem_limit(std::atomic<uint64_t> &done, Kernel *kernel, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
 
 // Activation-split workspace, one per (device, stream): calls on one stream
 // are ordered, so they can share it; calls on different streams cannot.
@@ -192,12 +210,8 @@ int make_tmap(CUtensorMap *map, CUtensorMapDataType dtype, int elem, const void 
 template <int QT, int BN, int NC, bool EPI>
 cudaError_t launch_tcdec_t(const CUtensorMap &tx, const DecArgs &a, int grid, cudaStream_t s) {
   using L = DecCfg<QT, BN>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(tcdec_kernel<QT, BN, NC, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<uint64_t> smem_set{0};
+  if (const cudaError_t e0 = raise_smem_limit(smem_set, tcdec_kernel<QT, BN, NC, EPI>, L::kAlloc)) return e0;
   const cudaError_t e = launch_pdl(tcdec_kernel<QT, BN, NC, EPI>, dim3(grid), dim3(L::kThreads), L::kAlloc, s, tx, a);
   count_launch();
   return e;
@@ -220,13 +234,8 @@ cudaError_t launch_tcdec_q(const CUtensorMap &tx, const DecArgs &a, int grid, in
 template <int QT, int BN, int STAGES>
 cudaError_t launch_gemm_t(const CUtensorMap &th, const CUtensorMap &tl, const GemmArgs &a, cudaStream_t s) {
   using L = GemmSmem<QT, BN, STAGES>;
-  static bool configured = false;  // per process; the attribute applies to every device
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<QT, BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         L::kAlloc);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<uint64_t> smem_set{0};
+  if (const cudaError_t e0 = raise_smem_limit(smem_set, gemm_kernel<QT, BN, STAGES>, L::kAlloc)) return e0;
   const dim3 grid((a.w.rows + kGemmRows - 1) / kGemmRows, (a.m + BN - 1) / BN);
   gemm_kernel<QT, BN, STAGES><<<grid, kGemmThreads, L::kAlloc, s>>>(th, tl, a);
   count_launch();
@@ -358,12 +367,8 @@ namespace {
 template <int QT, int MC>
 cudaError_t launch_sdec_t(const CUtensorMap &tx, const SdecArgs &a, int grid, cudaStream_t s) {
   using L = SdCfg<QT, MC>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(sdec_kernel<QT, MC>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<uint64_t> smem_set{0};
+  if (const cudaError_t e0 = raise_smem_limit(smem_set, sdec_kernel<QT, MC>, L::kAlloc)) return e0;
   const cudaError_t e = launch_pdl(sdec_kernel<QT, MC>, dim3(grid), dim3(kSdThreads), L::kAlloc, s, tx, a);
   count_launch();
   return e;
@@ -446,12 +451,8 @@ namespace {
 template <int QT, int MC, bool EPI>
 cudaError_t launch_i8dec_t(const I8Args &a, int grid, cudaStream_t s) {
   using L = I8Cfg<QT, MC>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(i8dec_kernel<QT, MC, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<uint64_t> smem_set{0};
+  if (const cudaError_t e0 = raise_smem_limit(smem_set, i8dec_kernel<QT, MC, EPI>, L::kAlloc)) return e0;
   const cudaError_t e = launch_pdl(i8dec_kernel<QT, MC, EPI>, dim3(grid), dim3(kI8Threads), L::kAlloc, s, a);
   count_launch();
   return e;

@@ -35,11 +35,24 @@ def quantized_bytes(qtype: int, rows: int, cols: int) -> int:
     return rows * ((cols + 31) // 32) * BLOCK_BYTES[qtype]
 
 
-def build(reference_root: str | None = None) -> None:
+# Where the read-only mini_ai checkout lives when the checker is built
+# (MINI_AI_REF overrides it); the GPU hosts only use the prebuilt files.
+DEFAULT_REFERENCE = "/root/reference"
+
+
+def reference_root() -> str | None:
+    root = os.environ.get("MINI_AI_REF") or DEFAULT_REFERENCE
+    return root if (Path(root) / "src" / "quantized_tensor.cc").exists() else None
+
+
+def build(reference_root_dir: str | None = None) -> None:
     """Compile the C restatement (and the reference build when its sources exist)."""
     env = dict(os.environ)
-    if reference_root:
-        env["REF"] = reference_root
+    root = reference_root_dir or reference_root()
+    if root:
+        env["REF"] = root
+    else:
+        env.pop("REF", None)
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True, env=env)
 
 
