@@ -206,10 +206,14 @@ int mq_linear_sharded_allgather(const mq_weight *shard, const float *x, int m, i
 
 /* Kernel selection for the next mq_linear calls on this thread:
  * 0 = automatic (default): the tcgen05 int8 decode GEMV for m <= 4, the
- *     tcgen05 fp16 decode GEMM for m <= 32, the tcgen05 prefill GEMM above;
+ *     tcgen05 scale-folded decode GEMM for m <= 32 (the fp16 decode GEMM for
+ *     weights whose block scales exceed the fold's fp16 range), the tcgen05
+ *     prefill GEMM above;
  * 1 = force the stream-K SIMT GEMV, 2 = force the tcgen05 prefill GEMM,
  * 3 = force the tcgen05 int8 decode GEMV, 4 = force the tcgen05 fp16 decode
- * GEMM (other values are ignored). Returns the previous mode. */
+ * GEMM, 5 = force the SIMT dp4a decode GEMV, 6 = force the tcgen05
+ * scale-folded decode GEMM (MQ_ERR_UNSUPPORTED for weights outside its
+ * range); other values are ignored. Returns the previous mode. */
 int mq_set_path(int mode);
 
 /* Number of kernels this library has launched in this process (all devices,

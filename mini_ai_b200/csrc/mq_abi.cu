@@ -124,9 +124,16 @@ int linear_dispatch(const mq_weight *w, const float *x, int m, int ldx, const fl
   if (mode == 1) return run_sdec(w, x, m, ldx, bias, y, ldy, s, gate, resid);
   if (mode == 3) return run_i8dec(w, x, m, ldx, bias, y, ldy, s, gate, resid);
   if (mode == 4) return run_tcdec(w, x, m, ldx, bias, y, ldy, s, gate, resid);
+  if (mode == 5) return run_gemv(w, x, m, ldx, bias, y, ldy, s, gate, resid);
+  if (mode == 6) {
+    if (!w->foldable)
+      return fail(MQ_ERR_UNSUPPORTED, "a block scale of this weight is too large for the scale-folded decode kernel");
+    return run_tcdec(w, x, m, ldx, bias, y, ldy, s, gate, resid, true);
+  }
   if (mode == 2 || (mode == 0 && m > decode_max_m())) return run_gemm(w, x, m, ldx, bias, y, ldy, s, gate, resid);
+  if (m <= gemv_max_m()) return run_gemv(w, x, m, ldx, bias, y, ldy, s, gate, resid);
   if (m <= i8dec_max_m()) return run_i8dec(w, x, m, ldx, bias, y, ldy, s, gate, resid);
-  return run_tcdec(w, x, m, ldx, bias, y, ldy, s, gate, resid);
+  return run_tcdec(w, x, m, ldx, bias, y, ldy, s, gate, resid, w->foldable);
 }
 
 }  // namespace
@@ -248,7 +255,10 @@ int mq_weight_shard_create(int device, int qtype, int rows, int cols, int row_be
   const size_t shard_src_bytes = (size_t)nrows * nb * bb;
   const uint8_t *src = static_cast<const uint8_t *>(blocks) + (size_t)row_begin * nb * bb;
   void *staging = nullptr;
+  int *unfoldable = nullptr, host_unfoldable = 1;
   e = cudaMemsetAsync(w->base, 0, total, s);
+  if (e == cudaSuccess) e = cudaMalloc(&unfoldable, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemsetAsync(unfoldable, 0, sizeof(int), s);
   if (e == cudaSuccess && !blocks_on_device) {
     e = cudaMalloc(&staging, shard_src_bytes);
     if (e == cudaSuccess) e = cudaMemcpyAsync(staging, src, shard_src_bytes, cudaMemcpyHostToDevice, s);
@@ -256,12 +266,15 @@ int mq_weight_shard_create(int device, int qtype, int rows, int cols, int row_be
   }
   if (e == cudaSuccess) {
     const int64_t n = (int64_t)nrows * nb;
-    repack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(src, w->v);
+    repack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(src, w->v, unfoldable);
     count_launch();
     e = cudaGetLastError();
   }
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&host_unfoldable, unfoldable, sizeof(int), cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (staging) cudaFree(staging);
+  if (unfoldable) cudaFree(unfoldable);
+  w->foldable = host_unfoldable == 0;
   if (e != cudaSuccess) {
     cudaFree(w->base);
     delete w;
@@ -315,7 +328,7 @@ int mq_weight_export(const mq_weight *w, void *dst, size_t dst_bytes) {
 
 int mq_set_path(int mode) {
   const int prev = g_path_mode;
-  if (mode >= 0 && mode <= 4) g_path_mode = mode;
+  if (mode >= 0 && mode <= 6) g_path_mode = mode;
   return prev;
 }
 

@@ -109,6 +109,13 @@ __device__ __forceinline__ float epilogue_out(float v, const float *gate, const 
   return v;
 }
 
+// Largest |d| for which every weight d * c (c = q - zp, |c| <= 8, 15, 128)
+// stays inside the fp16 range, so that the folded decode kernel
+// (mq_fdec.cuh) can hold it exactly as an fp16 hi + lo pair.
+__host__ __device__ constexpr float fold_max_scale(int qtype) {
+  return qtype == MQ_Q8_0 ? 65504.0f / 128.0f : qtype == MQ_Q4_1 ? 65504.0f / 16.0f : 65504.0f / 9.0f;
+}
+
 __host__ __device__ inline const uint8_t *chunk_ptr(const WeightView &w, int t, int k) {
   return w.base + ((int64_t)t * w.steps + k) * w.chunk_bytes;
 }
@@ -196,4 +203,5 @@ struct mq_weight {
   size_t bytes = 0;
   int row_begin = 0;          // first row of the full matrix (shards)
   int full_rows = 0;
+  bool foldable = false;      // every |d| < fold_max_scale: the folded decode kernel applies
 };

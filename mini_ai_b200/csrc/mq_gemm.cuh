@@ -312,8 +312,9 @@ bool gemm_supported(int device);
 // gate/up product: y = silu(gate) * product; residual add: y = resid + product).
 int run_sdec(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
              cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr);
+// folded: the scale-folded kernel (mq_fdec.cuh), for weights with mq_weight::foldable.
 int run_tcdec(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-              cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr);
+              cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr, bool folded = false);
 int run_gemm(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
              cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr);
 

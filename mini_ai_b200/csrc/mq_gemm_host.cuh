@@ -9,7 +9,9 @@
 #include <mutex>
 #include <utility>
 
+#include "mq_fdec.cuh"
 #include "mq_gemm.cuh"
+#include "mq_gemv.cuh"
 #include "mq_i8dec.cuh"
 #include "mq_sdec.cuh"
 #include "mq_tcdec.cuh"
@@ -22,13 +24,19 @@ namespace {
 // thread's current device only, so each launcher keeps one bit per device
 // (set once the attribute is in place there). Two host threads may both set
 // it on first use; that is harmless, and the mask itself is atomic.
+// `max_carveout` also asks for the largest shared-memory share of the unified
+// L1 / shared storage, for kernels sized to keep two CTAs on an SM.
 template <typename Kernel>
-cudaError_t raise_smem_limit(std::atomic<uint64_t> &done, Kernel *kernel, int bytes) {
+cudaError_t raise_smem_limit(std::atomic<uint64_t> &done, Kernel *kernel, int bytes, bool max_carveout = false) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
   if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  if (max_carveout) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
+  }
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
   return e;
@@ -231,6 +239,23 @@ cudaError_t launch_tcdec_q(const CUtensorMap &tx, const DecArgs &a, int grid, in
   return launch_tcdec_t<QT, 32, 32, false>(tx, a, grid, s);
 }
 
+template <int QT, int BN, bool EPI>
+cudaError_t launch_fdec_t(const CUtensorMap &tx, const DecArgs &a, int grid, cudaStream_t s) {
+  using L = FdCfg<QT, BN>;
+  static std::atomic<uint64_t> smem_set{0};
+  if (const cudaError_t e0 = raise_smem_limit(smem_set, fdec_kernel<QT, BN, BN, EPI>, L::kAlloc)) return e0;
+  const cudaError_t e = launch_pdl(fdec_kernel<QT, BN, BN, EPI>, dim3(grid), dim3(kFdThreads), L::kAlloc, s, tx, a);
+  count_launch();
+  return e;
+}
+
+template <int QT>
+cudaError_t launch_fdec_q(const CUtensorMap &tx, const DecArgs &a, int grid, int bn, cudaStream_t s) {
+  const bool epi = a.gate || a.resid;
+  if (bn == 16) return epi ? launch_fdec_t<QT, 16, true>(tx, a, grid, s) : launch_fdec_t<QT, 16, false>(tx, a, grid, s);
+  return epi ? launch_fdec_t<QT, 32, true>(tx, a, grid, s) : launch_fdec_t<QT, 32, false>(tx, a, grid, s);
+}
+
 template <int QT, int BN, int STAGES>
 cudaError_t launch_gemm_t(const CUtensorMap &th, const CUtensorMap &tl, const GemmArgs &a, cudaStream_t s) {
   using L = GemmSmem<QT, BN, STAGES>;
@@ -303,8 +328,8 @@ DecPlan tcdec_plan(const WeightView &w, int device, int max_grid) {
 
 int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const float *bias, float *y, int64_t ldy,
                  cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort, const float *gate,
-                 const float *resid) {
-  const int bn = dec_tile_rows(mm);
+                 const float *resid, bool folded) {
+  const int bn = folded ? fdec_tile_rows(mm) : dec_tile_rows(mm);
   MQ_CUDA(launch_pdl(dec_prep_kernel, dim3(plan.steps, (bn + 7) / 8), dim3(256), 0, s, x, ldx, mm, w.cols, plan.kpad,
                      bn, buf.x2, buf.xsum, buf.xinv, (int)(w.qtype == MQ_Q4_1)));
   count_launch();
@@ -315,18 +340,27 @@ int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const
   DecArgs a{w, mm, buf.xinv, buf.xsum, bias, y, ldy, buf.partial, buf.tickets, plan.steps, plan.tiles, buf.err,
             nan_on_abort, gate, resid};
   cudaError_t e;
-  switch (w.qtype) {
-  case MQ_Q8_0: e = launch_tcdec_q<MQ_Q8_0>(tx, a, plan.grid, mm, s); break;
-  case MQ_Q4_0: e = launch_tcdec_q<MQ_Q4_0>(tx, a, plan.grid, mm, s); break;
-  default: e = launch_tcdec_q<MQ_Q4_1>(tx, a, plan.grid, mm, s); break;
+  if (folded) {
+    switch (w.qtype) {
+    case MQ_Q8_0: e = launch_fdec_q<MQ_Q8_0>(tx, a, plan.grid, bn, s); break;
+    case MQ_Q4_0: e = launch_fdec_q<MQ_Q4_0>(tx, a, plan.grid, bn, s); break;
+    default: e = launch_fdec_q<MQ_Q4_1>(tx, a, plan.grid, bn, s); break;
+    }
+  } else {
+    switch (w.qtype) {
+    case MQ_Q8_0: e = launch_tcdec_q<MQ_Q8_0>(tx, a, plan.grid, mm, s); break;
+    case MQ_Q4_0: e = launch_tcdec_q<MQ_Q4_0>(tx, a, plan.grid, mm, s); break;
+    default: e = launch_tcdec_q<MQ_Q4_1>(tx, a, plan.grid, mm, s); break;
+    }
   }
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 decode launch");
   return MQ_OK;
 }
 
-// tcgen05 decode GEMM: up to 32 activation rows per launch (split + kernel).
+// tcgen05 decode GEMM: up to 32 activation rows per launch (split + kernel);
+// `folded` runs the scale-folded kernel (mq_fdec.cuh), which needs a foldable weight.
 int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-              cudaStream_t s, const float *gate, const float *resid) {
+              cudaStream_t s, const float *gate, const float *resid, bool folded) {
   int *err_dev = nullptr, *err_host = nullptr;
   int rc = err_flag(wt->device, &err_dev, &err_host);
   if (rc) return rc;
@@ -340,7 +374,7 @@ int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
   if ((rc = tickets_for(wt->device, s, (size_t)plan.tiles, &tickets))) return rc;
   for (int i0 = 0; i0 < m; i0 += 32) {
     const int mm = std::min(32, m - i0);
-    const int bn = dec_tile_rows(mm);
+    const int bn = folded ? fdec_tile_rows(mm) : dec_tile_rows(mm);
     const size_t xbytes = (size_t)2 * bn * plan.kpad * 2;
     const size_t sbytes = (size_t)(plan.kpad / 32) * bn * 4;
     const size_t ibytes = ((size_t)plan.steps * bn * 4 + 255) & ~size_t(255);
@@ -356,7 +390,8 @@ int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
     buf.tickets = tickets;
     buf.err = err_dev;
     if ((rc = tcdec_launch(w, x + (int64_t)i0 * ldx, mm, ldx, bias, y + (int64_t)i0 * ldy, ldy, s, plan, buf, 0,
-                           gate ? gate + (int64_t)i0 * ldy : nullptr, resid ? resid + (int64_t)i0 * ldy : nullptr)))
+                           gate ? gate + (int64_t)i0 * ldy : nullptr, resid ? resid + (int64_t)i0 * ldy : nullptr,
+                           folded)))
       return rc;
   }
   return MQ_OK;
@@ -509,6 +544,66 @@ int run_i8dec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
     default: e = launch_i8dec_q<MQ_Q4_1>(a, plan.grid, mc, s); break;
     }
     if (e != cudaSuccess) return cuda_fail(e, "int8 decode launch");
+  }
+  return MQ_OK;
+}
+
+namespace {
+
+template <int QT, int MC, bool EPI>
+cudaError_t launch_gemv_t(const GvArgs &a, int grid, cudaStream_t s) {
+  using L = GvCfg<QT, MC>;
+  static std::atomic<uint64_t> smem_set{0};
+  if (const cudaError_t e0 = raise_smem_limit(smem_set, gemv_kernel<QT, MC, EPI>, L::kBytes, true)) return e0;
+  const cudaError_t e = launch_pdl(gemv_kernel<QT, MC, EPI>, dim3(grid), dim3(kGvThreads), L::kBytes, s, a);
+  count_launch();
+  return e;
+}
+
+template <int QT>
+cudaError_t launch_gemv_q(const GvArgs &a, int grid, int mc, cudaStream_t s) {
+  if (a.gate || a.resid) return mc == 1 ? launch_gemv_t<QT, 1, true>(a, grid, s) : launch_gemv_t<QT, 2, true>(a, grid, s);
+  return mc == 1 ? launch_gemv_t<QT, 1, false>(a, grid, s) : launch_gemv_t<QT, 2, false>(a, grid, s);
+}
+
+}  // namespace
+
+// Largest activation count served by the SIMT dp4a GEMV in automatic mode
+// (mq_gemv.cuh); it takes up to 2 rows per launch.
+int gemv_max_m() {
+  static const int v = env_threshold("MQ_GEMV_MAX_M", 0);
+  return v;
+}
+
+// SIMT dp4a decode GEMV: up to 2 activation rows per launch.
+int run_gemv(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
+             cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr) {
+  int *err_dev = nullptr, *err_host = nullptr;
+  int rc = err_flag(wt->device, &err_dev, &err_host);
+  if (rc) return rc;
+  if (*(volatile int *)err_host) {
+    *(volatile int *)err_host = 0;
+    return fail(MQ_ERR_TIMEOUT, "an earlier decode launch on device %d ran out of a bounded wait", wt->device);
+  }
+  const WeightView &w = wt->v;
+  const DecPlan plan = tcdec_plan(w, wt->device);
+  int *tickets = nullptr;
+  if ((rc = tickets_for(wt->device, s, (size_t)plan.tiles, &tickets))) return rc;
+  for (int i0 = 0; i0 < m; i0 += 2) {
+    const int mm = std::min(2, m - i0);
+    const size_t pbytes = (size_t)plan.grid * 2 * kGvRows * mm * 4;
+    void *ws = nullptr;
+    if ((rc = workspace_for(wt->device, s, pbytes + 1024, &ws))) return rc;
+    GvArgs a{w, mm, x + (int64_t)i0 * ldx, ldx, bias, y + (int64_t)i0 * ldy, ldy, static_cast<float *>(ws), tickets,
+             plan.steps, plan.tiles, err_dev, 0, gate ? gate + (int64_t)i0 * ldy : nullptr,
+             resid ? resid + (int64_t)i0 * ldy : nullptr};
+    cudaError_t e;
+    switch (w.qtype) {
+    case MQ_Q8_0: e = launch_gemv_q<MQ_Q8_0>(a, plan.grid, mm, s); break;
+    case MQ_Q4_0: e = launch_gemv_q<MQ_Q4_0>(a, plan.grid, mm, s); break;
+    default: e = launch_gemv_q<MQ_Q4_1>(a, plan.grid, mm, s); break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "dp4a decode launch");
   }
   return MQ_OK;
 }

@@ -14,12 +14,18 @@
 namespace mq {
 
 // GGUF block stream (rows x nb blocks, starting at `src`) -> step chunks.
-__global__ void repack_kernel(const uint8_t *__restrict__ src, WeightView w) {
+// `unfoldable` (optional) is raised when a block scale is not finite or so
+// large that d * c leaves the fp16 range (the folded decode kernel, mq_fdec.cuh).
+__global__ void repack_kernel(const uint8_t *__restrict__ src, WeightView w, int *unfoldable = nullptr) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)w.rows * w.nb) return;
   const int r = (int)(i / w.nb), b = (int)(i % w.nb);
   const int bb = block_bytes(w.qtype), qb = block_qbytes(w.qtype), hdr = bb - qb;
   const uint8_t *blk = src + i * bb;
+  if (unfoldable) {
+    const float d = fabsf(f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8))));
+    if (!(d < fold_max_scale(w.qtype))) atomicOr(unfoldable, 1);
+  }
   const int rr = r % kTileRows, jb = b % kStepBlocks;
   uint8_t *c = const_cast<uint8_t *>(chunk_ptr(w, r / kTileRows, b / kStepBlocks));
   uint8_t *sc = c + w.pk_bytes + rr * 16 + 2 * jb;

@@ -30,14 +30,17 @@ struct DecBuffers {
 DecPlan tcdec_plan(const WeightView &w, int device, int max_grid = 0);
 
 inline int dec_tile_rows(int m) { return m <= 8 ? 8 : (m <= 16 ? 16 : 32); }
+// Activation tile height of the scale-folded decode kernel (mq_fdec.cuh): 16 or 32.
+inline int fdec_tile_rows(int m) { return m <= 16 ? 16 : 32; }
 
 // One launch pair (activation split + decode GEMM) for m <= 32 rows; bn (the
 // activation tile height, dec_tile_rows) is 8 for m <= 8, 16 for m <= 16, else
 // 32. nan_on_abort: a timed-out bounded wait writes NaN to the outputs instead
-// of leaving them unwritten.
+// of leaving them unwritten. folded: the scale-folded kernel (mq_fdec.cuh; bn
+// from fdec_tile_rows), for weights whose scales allow the fold.
 int tcdec_launch(const WeightView &w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
                  cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort,
-                 const float *gate = nullptr, const float *resid = nullptr);
+                 const float *gate = nullptr, const float *resid = nullptr, bool folded = false);
 
 bool gemm_supported(int device);
 

@@ -209,7 +209,8 @@ def test_dimension_mismatch_raises(mq, cuda_device):
     assert "CUDA devices=" in mq.CudaDeviceInfo()
 
 
-PATHS = {1: "streamk_simt_gemv", 3: "tcgen05_i8_decode", 4: "tcgen05_decode", 2: "tcgen05_gemm"}
+PATHS = {1: "streamk_simt_gemv", 3: "tcgen05_i8_decode", 4: "tcgen05_decode", 2: "tcgen05_gemm", 5: "simt_dp4a_gemv",
+         6: "tcgen05_folded_decode"}
 
 
 @pytest.mark.parametrize("path", sorted(PATHS), ids=lambda p: PATHS[p])
@@ -218,7 +219,7 @@ def test_every_path_against_oracle(mq, oracle, cuda_device, path, q):
     """Each kernel, forced, on odd shapes: tail blocks (K % 32), row tails
     (N % 16, N % 128), activation counts around every tile edge."""
     ms = {1: [1, 2, 3, 4, 5, 9], 3: [1, 2, 3, 4, 5, 9], 4: [1, 2, 4, 5, 8, 9, 16, 17, 32, 33],
-          2: [1, 7, 128, 129, 300]}[path]
+          2: [1, 7, 128, 129, 300], 5: [1, 2, 3, 5], 6: [1, 5, 8, 9, 16, 17, 32, 33]}[path]
     for rows, cols in [(300, 4097), (136, 320), (1000, 96)]:
         for m in ms:
             s, x, y_ref, bound = _llama_case(mq, oracle, q, rows, cols, m, seed=rows * 7 + m + path)
@@ -259,7 +260,8 @@ def test_swiglu_gate_up_against_oracle(mq, oracle, cuda_device, path, q):
     shapes (tail blocks, row tails) and activation counts across the automatic path's regimes.
     Tolerance: the linear parity bound carried through silu (|silu'| < 1.1)."""
     torch = _torch()
-    ms = {0: [1, 3, 16, 40], 1: [1, 3, 5], 3: [1, 2, 4, 5], 4: [1, 5, 16, 33], 2: [1, 129]}[path]
+    ms = {0: [1, 3, 16, 40], 1: [1, 3, 5], 3: [1, 2, 4, 5], 4: [1, 5, 16, 33], 2: [1, 129], 5: [1, 2, 3],
+          6: [5, 16, 32]}[path]
     for rows, cols in [(300, 4097), (1024, 4096)]:
         for m in ms:
             sg, x, g_ref, bg = _llama_case(mq, oracle, q, rows, cols, m, seed=rows * 3 + m + path * 11)
@@ -307,7 +309,8 @@ def test_residual_add_against_oracle(mq, oracle, cuda_device, path, q):
     AddKernel, src/cuda_backend.cu:236-240), in place and out of place, through every kernel:
     within the parity bound of the oracle, and bit-identical to the unfused product plus the add."""
     torch = _torch()
-    ms = {0: [1, 3, 16, 40], 1: [1, 3, 5], 3: [1, 2, 4, 5], 4: [1, 5, 16, 33], 2: [1, 129]}[path]
+    ms = {0: [1, 3, 16, 40], 1: [1, 3, 5], 3: [1, 2, 4, 5], 4: [1, 5, 16, 33], 2: [1, 129], 5: [1, 2, 3],
+          6: [5, 16, 32]}[path]
     for rows, cols in [(300, 4097), (1024, 4096)]:
         for m in ms:
             s, x, y_ref, bound = _llama_case(mq, oracle, q, rows, cols, m, seed=rows * 17 + m + path * 7)
@@ -329,3 +332,30 @@ def test_residual_add_against_oracle(mq, oracle, cuda_device, path, q):
             assert_linear_close(y.cpu().numpy(), ref, bound)
             assert torch.equal(y, unfused) and torch.equal(inplace, y)
             w.close()
+
+
+def test_large_scales_fall_back_from_the_folded_kernel(mq, oracle, cuda_device):
+    """Weights whose block scales would overflow fp16 once folded into the codes
+    (|d * c| >= 65504: here Q8_0 blocks of magnitude ~1e5, d ~ 790) run on the
+    unfolded fp16 decode kernel in automatic mode, and the folded kernel refuses
+    them when forced; results stay within the parity bound."""
+    torch = _torch()
+    rng = np.random.default_rng(65504)
+    rows, cols, m = 256, 512, 16
+    w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+    w[7, 40] = 1.0e5
+    w[200, 300] = -0.9e5
+    s = mq.QuantizeTensor(w, Q8_0)
+    x = rng.standard_normal((m, cols)).astype(np.float32)
+    y_ref = oracle.linear(Q8_0, s.bytes, rows, cols, x, threads=THREADS)
+    bound = abs_dot_bound(oracle.dequantize(Q8_0, s.bytes, rows, cols), x)
+    assert_linear_close(gpu_linear(mq, s, x, cuda_device, path=0), y_ref, bound)
+    dw = mq.CudaWeight(s, device=cuda_device)
+    prev = mq.set_path(6)
+    try:
+        with pytest.raises(mq.MQError, match="too large for the scale-folded"):
+            dw.linear(dev(x, cuda_device))
+    finally:
+        mq.set_path(prev)
+    torch.cuda.synchronize(cuda_device)
+    dw.close()
