@@ -189,6 +189,11 @@ int mq_comm_unique_id(void *id, size_t len);
 int mq_comm_create(int device, int nranks, int rank, const void *id, size_t len, mq_comm **out);
 void mq_comm_destroy(mq_comm *c);
 
+/* 1 when the communicator gathers over NVLink peer memory (MQ_P2P_GATHER=1
+ * and every rank mapped every peer), 0 when it uses NCCL's all-gather, a
+ * negative code for a NULL handle. */
+int mq_comm_uses_peer_gather(const mq_comm *c);
+
 /* y[i, n] for all n in [0, N) on every rank: this rank's shard product
  * (+ bias[rank*R .. rank*R+R) when bias, the full [N] vector, is given) and
  * an all-gather of the slices. x: device F32 [m, ldx] (full K); y: device F32

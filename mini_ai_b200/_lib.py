@@ -43,6 +43,7 @@ SIGNATURES = {
     "mq_comm_unique_id": (_i, [_vp, _sz]),
     "mq_comm_create": (_i, [_i, _i, _i, _vp, _sz, C.POINTER(_vp)]),
     "mq_comm_destroy": (None, [_vp]),
+    "mq_comm_uses_peer_gather": (_i, [_vp]),
     "mq_linear_sharded_allgather": (_i, [_vp, _vp, _i, _i, _vp, _vp, _i, _vp, _vp]),
     "mq_set_path": (_i, [_i]),
     "mq_kernel_launches": (C.c_uint64, []),

@@ -446,6 +446,11 @@ int mq_comm_create(int device, int nranks, int rank, const void *id, size_t len,
   return MQ_OK;
 }
 
+int mq_comm_uses_peer_gather(const mq_comm *c) {
+  if (!c) return mq::fail(MQ_ERR_INVALID, "null comm handle");
+  return c->p2p ? 1 : 0;
+}
+
 void mq_comm_destroy(mq_comm *c) {
   if (!c) return;
   int prev = -1;

@@ -68,6 +68,14 @@ class CudaComm:
         dist.broadcast_object_list(obj, src=0, group=group)
         return cls(device, world, rank, obj[0])
 
+    @property
+    def uses_peer_gather(self) -> bool:
+        """True when the gather runs over NVLink peer memory, False when over NCCL."""
+        rc = lib().mq_comm_uses_peer_gather(self.handle)
+        if rc < 0:
+            check(rc, "mq_comm_uses_peer_gather")
+        return rc == 1
+
     def close(self) -> None:
         if getattr(self, "handle", None):
             lib().mq_comm_destroy(self.handle)

@@ -142,3 +142,21 @@ def test_two_ranks_allgather(gather):
     res = subprocess.run(["timeout", "-k", "30", "300", *cmd], capture_output=True, text=True, env=env, cwd=ROOT)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     assert res.stdout.count("sharded ok") == 2
+
+
+@pytest.mark.gpu
+def test_two_ranks_peer_gather_timeout():
+    """A rank that leaves out a call: the other rank's peer-memory gather gives up
+    after its wait limit (0.2 s here), writes NaN into the missing columns and
+    reports MQ_ERR_TIMEOUT from then on (tests/timeout_worker.py). Two GPUs."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MQ_P2P_GATHER="1", MQ_P2P_WAIT_NS="200000000")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1",
+           f"--master-port={_free_port()}", str(ROOT / "tests" / "timeout_worker.py")]
+    res = subprocess.run(["timeout", "-k", "30", "300", *cmd], capture_output=True, text=True, env=env, cwd=ROOT)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
+    out = res.stdout
+    assert out.count("timeout ok") == 2 or out.count("timeout check skipped") == 2, out[-3000:]
