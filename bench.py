@@ -388,7 +388,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": wl["unit"], "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6), "higher_is_better": True,
-            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "scaling": "strong", "vs_baseline": None,
             "dtype": "f32 (GGUF " + "/".join(sorted({TNAME[p[0]].upper() for p in prods})) + " weights)",
             "data": "synthetic (seeded N(0,0.02) weights packed bit-exactly, N(0,1) activations)",
             "config": {"workload": args.workload + (f" (class {args.only})" if args.only else ""),
@@ -660,7 +660,7 @@ def run_reference(args, rank: int, world: int) -> None:
     unit = wl["unit"]
     out = {"metric": METRIC, "value": round(value, 6), "unit": unit, "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": round(total_t / args.steps * 1e3, 3), "higher_is_better": True,
-           "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+           "scaling": "strong", "vs_baseline": None,
            "dtype": "f32 (GGUF " + "/".join(sorted({TNAME[p[0]].upper() for p in prods})) + " weights)",
            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)", "impl": "reference",
            "config": {"workload": args.workload + (f" (class {args.only})" if args.only else ""),

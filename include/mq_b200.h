@@ -228,6 +228,13 @@ uint64_t mq_kernel_launches(void);
 /* Human-readable device list, like CudaDeviceInfo (src/cuda_backend.cu:355-369). */
 int mq_device_info(char *buf, size_t len);
 
+/* The bounded-wait error flag of `device` as its kernels see it: a device
+ * pointer to an int in mapped host memory. A tensor-core kernel whose wait ran
+ * out stores 1 there; the next tensor-core call on that device then returns
+ * MQ_ERR_TIMEOUT and clears it. Exposed so that a monitor or a test can read
+ * the flag or raise it from the device (cudaMemset, or a kernel's store). */
+int mq_device_error_flag(int device, int **flag);
+
 #ifdef __cplusplus
 }
 #endif

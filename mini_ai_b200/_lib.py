@@ -48,6 +48,7 @@ SIGNATURES = {
     "mq_set_path": (_i, [_i]),
     "mq_kernel_launches": (C.c_uint64, []),
     "mq_device_info": (_i, [C.c_char_p, _sz]),
+    "mq_device_error_flag": (_i, [_i, C.POINTER(_vp)]),
 }
 
 _lock = threading.Lock()

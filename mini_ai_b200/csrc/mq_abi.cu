@@ -398,6 +398,17 @@ int mq_linear_ragged(const mq_weight *w, const float *x, const int *offsets, int
 
 uint64_t mq_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
+int mq_device_error_flag(int device, int **flag) {
+  last_error().clear();
+  if (!flag) return fail(MQ_ERR_INVALID, "null output pointer");
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count)
+    return fail(MQ_ERR_INVALID, "device %d is not a CUDA device of this process", device);
+  DeviceGuard guard(device);
+  int *host = nullptr;
+  return device_err_flag(device, flag, &host);
+}
+
 int mq_device_info(char *buf, size_t len) {
   last_error().clear();
   if (!buf || !len) return fail(MQ_ERR_INVALID, "null buffer");

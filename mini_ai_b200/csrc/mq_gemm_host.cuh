@@ -330,8 +330,12 @@ int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const
                  cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort, const float *gate,
                  const float *resid, bool folded) {
   const int bn = folded ? fdec_tile_rows(mm) : dec_tile_rows(mm);
-  MQ_CUDA(launch_pdl(dec_prep_kernel, dim3(plan.steps, (bn + 7) / 8), dim3(256), 0, s, x, ldx, mm, w.cols, plan.kpad,
-                     bn, buf.x2, buf.xsum, buf.xinv, (int)(w.qtype == MQ_Q4_1)));
+  if (folded)  // one scale per activation row: the folded kernel accumulates along K
+    MQ_CUDA(launch_pdl(fold_prep_kernel, dim3(bn, (plan.steps + kFpSteps - 1) / kFpSteps), dim3(kFpThreads), 0, s,
+                       x, ldx, mm, w.cols, plan.kpad, bn, buf.x2, buf.xsum, buf.xinv, (int)(w.qtype == MQ_Q4_1)));
+  else
+    MQ_CUDA(launch_pdl(dec_prep_kernel, dim3(plan.steps, (bn + 7) / 8), dim3(256), 0, s, x, ldx, mm, w.cols,
+                       plan.kpad, bn, buf.x2, buf.xsum, buf.xinv, (int)(w.qtype == MQ_Q4_1)));
   count_launch();
   CUtensorMap tx;
   int rc;

@@ -90,7 +90,7 @@ constexpr uint64_t kDecDrainNs = 20000000ull;
 struct DecArgs {
   WeightView w;
   int m;                 // activation rows (<= NC)
-  const float *xinv;     // [steps][BN] 2^-e per (step, activation row)
+  const float *xinv;     // [steps][BN] 2^-e per (step, activation row); folded kernel: [BN] per row
   const float *xsum;     // [kpad / 32][BN] scaled block sums of x (Q4_1)
   const float *bias;
   float *y;

@@ -20,7 +20,7 @@ struct DecPlan {
 struct DecBuffers {
   __half *x2;         // [2 bn][kpad]: activation rows split into fp16 hi rows, then lo rows
   float *xsum;        // [kpad / 32][bn]: scaled block sums of x (Q4_1)
-  float *xinv;        // [steps][bn]: 2^-e per (256-K step, activation row)
+  float *xinv;        // [steps][bn]: 2^-e per (256-K step, activation row); folded kernel: [bn], per row
   float *partial;     // [grid][2][128][bn]: head / tail partial tile of every CTA
   int *tickets;       // [tiles], zero between launches
   int *err;           // device-visible timeout flag

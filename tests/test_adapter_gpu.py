@@ -12,8 +12,15 @@ The suite's CUDA test (tests/test_cuda.cc:9-49) is the parity check of the
 boundary: the tiny model (hidden 86: tail blocks) with normal and NeoX RoPE,
 q/k/v biases, and F32, Q8_0, Q4_0 and Q4_1 weights (QuantizeModel), five
 tokens through ForwardToken on the CPU and through the B200 backend, every
-logit within 1e-4. The other 152 tests check that linking the backend leaves
-the rest of mini_ai unchanged.
+logit within 1e-4. The other 152 tests of the reference's suite check that
+linking the backend leaves the rest of mini_ai unchanged.
+
+Four more tests in the same runner (mini_ai_b200/adapter/test_b200_backend.cc)
+cover the backend's surface beyond backend.h: the batched forward of several
+ragged requests against the CPU ForwardBatch (decode kernels and the prefill
+GEMM), its input checks, QuantizeModelB200 against QuantizeModel, and a GGUF
+file with Q8_0 / Q4_0 / Q4_1 linears loaded by the reference's loader and run
+on the device.
 """
 from __future__ import annotations
 
@@ -35,7 +42,10 @@ def test_reference_suite_with_b200_backend():
     out = res.stdout + res.stderr
     assert "[PASS] cuda_backend_availability_and_forward" in out, out[-4000:]
     assert res.returncode == 0, out[-4000:]
-    assert "Results: 153 passed, 0 failed" in out, out[-2000:]
+    for name in ("b200_batched_forward_matches_cpu", "b200_batched_forward_rejects_bad_input",
+                 "b200_quantize_model_matches_reference", "b200_gguf_quantized_model_forward"):
+        assert f"[PASS] {name}" in out, out[-4000:]
+    assert "Results: 157 passed, 0 failed" in out, out[-2000:]
     # CudaStats after each (layout, type) case: weights went through the backend.
     stats = [line for line in out.splitlines() if line.startswith("uploaded_weights=")]
     assert len(stats) == 8 and all("cuda_linear_calls=" in s for s in stats), stats
