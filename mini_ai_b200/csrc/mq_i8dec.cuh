@@ -8,18 +8,19 @@
 //           = sum_b d[n,b] * sum_k (q - 8) * x                (Q4_0: q unsigned)
 //           = sum_b (d[n,b] * sum_k q * x + m[n,b] * sum_k x) (Q4_1)
 //
-// Exactness scheme. Each activation row is scaled, per 256-K step, by a
-// power of two 2^e so that its largest magnitude lies in [2^21, 2^22), and
-// rounded to an integer X (22 significant bits: the rounding error is below
-// 2^-22 of the step's largest |x|). X is split into three signed 8-bit limbs,
+// Exactness scheme. Each activation row is scaled, per 32-element quant
+// block, by a power of two 2^e so that the block's largest magnitude lies in
+// [2^21, 2^22), and rounded to an integer X (22 significant bits: the
+// rounding error of an element is at most 2^-22 of the largest |x| of its
+// block, so an outlier costs precision only inside its own block). X is split into three signed 8-bit limbs,
 // X = l2 * 2^16 + l1 * 2^8 + l0, and the limbs are the rows of the MMA's B
 // operand (row 3t + l for activation row t, limb l). One tcgen05.mma of
 // kind::i8 (M = 128 weight rows, N = 16, K = 32 = one quant block) gives, per
 // weight row and block, the exact int32 sums L_l = sum_k q * l_l. The drainer
 // warps combine the limbs (in int32 for Q4_x, where |sum q X| < 2^31, so the
-// wrapping sum is exact; in fp32 for Q8_0) and apply the fp16 block scale in
-// fp32, and 2^-e once per step, so the result equals the reference's fp32 dot
-// up to accumulation-order rounding.
+// wrapping sum is exact; in fp32 for Q8_0) and apply the fp16 block scale and
+// the block's 2^-e in fp32, so the result equals the reference's fp32 dot up
+// to that rounding and accumulation order.
 //
 // Data flow per (128-row tile, 8-block step):
 //   weight chunk (packed codes, fp16 scales, Q4_1 mins; consecutive in
@@ -90,8 +91,8 @@ constexpr int kI8Threads = kI8Warps * 32;
 constexpr int kI8MaxM = 5;          // activation rows per launch: 3 limbs x 5 rows <= N = 16
 constexpr int kI8N = 16;            // MMA N (B rows)
 constexpr int kI8BTile = 4096;      // B tile of a step: 2 slabs x 16 rows x 128 B (128-byte swizzle)
-constexpr int kI8HdrInv = 0;        // header: 2^-e per activation row, float[8]
-constexpr int kI8HdrSx = 32;        // header: integer block sums of X, int32[8 blocks][8 rows]
+constexpr int kI8HdrInv = 0;        // header: 2^-e per (block, activation row), float[8 blocks][8 rows]
+constexpr int kI8HdrSx = 256;       // header: integer block sums of X, int32[8 blocks][8 rows]
 constexpr int kI8Done = 8;          // commit barriers (ring)
 constexpr uint64_t kI8WaitNs = 1000000000ull;
 constexpr uint64_t kI8DrainNs = 20000000ull;
@@ -293,12 +294,13 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
     }
   } else if (warp >= 4 && warp < 4 + kI8Preps) {  // ---------- prep: activation slice -> limb tile + header
     // Lane l builds the 4-slot words w = l and l + 32 of each limb row (word
-    // w: block w / 8, A column w % 8). A row's slice is scaled by 2^e (largest
-    // magnitude in [2^21, 2^22)) and rounded to integers X (round to nearest
-    // even through the fp32 magic 1.5 * 2^23), split into balanced limbs
-    // X = l0 + 2^8 l1 + 2^16 l2; the header holds 2^-e and the integer block
-    // sums of X. A non-finite value in the slice makes 2^-e NaN, so that row's
-    // outputs become NaN.
+    // w: block w / 8, A column w % 8), so lanes 8i..8i+7 hold block i (u = 0)
+    // and block 4 + i (u = 1). Each block of a row is scaled by its own 2^e
+    // (largest magnitude in [2^21, 2^22)) and rounded to integers X (round to
+    // nearest even through the fp32 magic 1.5 * 2^23), split into balanced
+    // limbs X = l0 + 2^8 l1 + 2^16 l2; the header holds 2^-e and the integer
+    // sum of X of every (block, row). A non-finite value in a block makes its
+    // 2^-e NaN, so that row's outputs become NaN.
     const int pw = warp - 4;
     auto word_off = [](int n, int w) {  // byte offset of word w of B row n inside a limb tile
       const int j = w >> 3, c8 = w & 7;
@@ -356,54 +358,52 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
       int *sx = reinterpret_cast<int *>(hdr + kI8HdrSx);
 #pragma unroll
       for (int t = 0; t < MC; ++t) {
-        uint32_t mb = 0u;  // largest |x| bits (integer order = magnitude order, NaN above Inf)
-#pragma unroll
-        for (int q = 0; q < 8; ++q) mb = max(mb, __float_as_uint(v[t][q]) & 0x7fffffffu);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
-        const bool finite = mb < 0x7f800000u;
-        // mx = f * 2^E with f in [0.5, 1): E = biased exponent - 126 (subnormal slices use E = -125)
-        const int be = (int)(mb >> 23);
-        const int e = (mb == 0u || !finite) ? 0 : min(126, max(-126, 22 - ((be > 0 ? be : 1) - 126)));
-        const float sc = __uint_as_float((uint32_t)(127 + e) << 23);
-        int X[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          X[q] = finite ? (int)(__float_as_uint(fmaf(v[t][q], sc, 12582912.0f)) - 0x4B400000u) : 0;
+        // The lane's two blocks one at a time (u = 0: block lane / 8, u = 1: block
+        // 4 + lane / 8), so that only one block's values are live.
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
+          uint32_t mb = 0u;  // largest |x| bits (integer order = magnitude order, NaN above Inf)
+#pragma unroll
+          for (int p = 0; p < 4; ++p) mb = max(mb, __float_as_uint(v[t][4 * u + p]) & 0x7fffffffu);
+#pragma unroll
+          for (int o = 4; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));  // the block's 8 lanes
+          const bool finite = mb < 0x7f800000u;
+          // mx = f * 2^E with f in [0.5, 1): E = biased exponent - 126 (subnormal blocks use E = -125)
+          const int be = (int)(mb >> 23);
+          const int e = (mb == 0u || !finite) ? 0 : min(126, max(-126, 22 - ((be > 0 ? be : 1) - 126)));
+          const float sc = __uint_as_float((uint32_t)(127 + e) << 23);
           const int w = lane + 32 * u;
-          uint32_t b0[4], b1[4], b2[4];
+          uint32_t b0 = 0u, b1 = 0u, b2 = 0u;
+          int sum = 0;
 #pragma unroll
           for (int p = 0; p < 4; ++p) {
-            const int xv = X[4 * u + p];
+            const int xv = finite ? (int)(__float_as_uint(fmaf(v[t][4 * u + p], sc, 12582912.0f)) - 0x4B400000u) : 0;
             const int x1 = (xv - (int)(int8_t)xv) >> 8;  // balanced: l0 = sext(low byte)
             const int l2 = (x1 - (int)(int8_t)x1) >> 8;
-            b0[p] = (uint32_t)xv & 255u, b1[p] = (uint32_t)x1 & 255u, b2[p] = (uint32_t)l2 & 255u;
+            b0 |= ((uint32_t)xv & 255u) << (8 * p);
+            b1 |= ((uint32_t)x1 & 255u) << (8 * p);
+            b2 |= ((uint32_t)l2 & 255u) << (8 * p);
+            sum += xv;
           }
           // rows of this word's block; with block pairs, zeros in the partner block's rows
           const int rb = ((w >> 3) % L::G) * L::kRowOff + 3 * t;
-          *reinterpret_cast<uint32_t *>(tile + word_off(rb + 0, w)) = b0[0] | (b0[1] << 8) | (b0[2] << 16) | (b0[3] << 24);
-          *reinterpret_cast<uint32_t *>(tile + word_off(rb + 1, w)) = b1[0] | (b1[1] << 8) | (b1[2] << 16) | (b1[3] << 24);
-          *reinterpret_cast<uint32_t *>(tile + word_off(rb + 2, w)) = b2[0] | (b2[1] << 8) | (b2[2] << 16) | (b2[3] << 24);
+          *reinterpret_cast<uint32_t *>(tile + word_off(rb + 0, w)) = b0;
+          *reinterpret_cast<uint32_t *>(tile + word_off(rb + 1, w)) = b1;
+          *reinterpret_cast<uint32_t *>(tile + word_off(rb + 2, w)) = b2;
           if constexpr (L::G == 2) {
             const int rz = (1 - ((w >> 3) & 1)) * L::kRowOff + 3 * t;
 #pragma unroll
             for (int l = 0; l < 3; ++l) *reinterpret_cast<uint32_t *>(tile + word_off(rz + l, w)) = 0u;
           }
-        }
-        // integer block sums: word w of lane l belongs to block w / 8 = lane / 8 (+ 4)
-        int s0 = X[0] + X[1] + X[2] + X[3], s1 = X[4] + X[5] + X[6] + X[7];
+          // integer block sum over the block's 8 lanes, and the block's 2^-e
 #pragma unroll
-        for (int o = 4; o > 0; o >>= 1) {
-          s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-          s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+          for (int o = 4; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+          if ((lane & 7) == 0) {
+            const int j = 4 * u + (lane >> 3);
+            sx[j * 8 + t] = sum;
+            inv[j * 8 + t] = finite ? __uint_as_float((uint32_t)(127 - e) << 23) : __int_as_float(0x7fc00000);
+          }
         }
-        if ((lane & 7) == 0) {
-          sx[(lane >> 3) * 8 + t] = s0;
-          sx[(4 + (lane >> 3)) * 8 + t] = s1;
-        }
-        if (lane == 0) inv[t] = finite ? __uint_as_float((uint32_t)(127 - e) << 23) : __int_as_float(0x7fc00000);
       }
       sm100::fence_proxy_async_smem();  // the MMAs read the tile through the async proxy
       __syncwarp();
@@ -620,7 +620,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
         const float *inv = reinterpret_cast<const float *>(dr + L::kDrHdr + kI8HdrInv);
         const int *sx = reinterpret_cast<const int *>(dr + L::kDrHdr + kI8HdrSx);
         const uint32_t dbase = tmem + lane_base + (uint32_t)(L::kDOff + (ls % ND) * L::kDCols);
-        float st[MC];  // this step's sum, in the step's activation scale
+        float st[MC];  // this step's sum
 #pragma unroll
         for (int c = 0; c < MC; ++c) st[c] = 0.0f;
         constexpr int kRegions = 8 / L::G;
@@ -651,27 +651,39 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
               mn = (j & 1) ? __high2float(m2) : __low2float(m2);
             }
             const uint32_t *vb = &v[(jb / L::G) * NCOL + (jb % L::G) * L::kRowOff];
+            float bis[MC];  // the block's 2^-e of every activation row: exact scaling
+            if constexpr (MC >= 4) {
+#pragma unroll
+              for (int c = 0; c < MC; c += 4) {
+                const float4 b4 = *reinterpret_cast<const float4 *>(inv + j * 8 + c);
+                bis[c] = b4.x, bis[c + 1] = b4.y, bis[c + 2] = b4.z, bis[c + 3] = b4.w;
+              }
+            } else {
+#pragma unroll
+              for (int c = 0; c < MC; ++c) bis[c] = inv[j * 8 + c];
+            }
 #pragma unroll
             for (int c = 0; c < MC; ++c) {
               const int l0 = (int)vb[3 * c], l1 = (int)vb[3 * c + 1], l2 = (int)vb[3 * c + 2];
+              const float bi = bis[c];
               if constexpr (QT == MQ_Q8_0) {
                 const int v01 = l0 + (int)((uint32_t)l1 << 8);  // |.| < 2^27: exact
-                st[c] = fmaf(d, fmaf((float)l2, 65536.0f, (float)v01), st[c]);
+                st[c] = fmaf(d * fmaf((float)l2, 65536.0f, (float)v01), bi, st[c]);
               } else {
                 // sum q * X fits int32, so the wrapping combination is exact.
                 int vv = (int)((uint32_t)l0 + ((uint32_t)l1 << 8) + ((uint32_t)l2 << 16));
                 if constexpr (QT == MQ_Q4_0) {
                   vv = (int)((uint32_t)vv - ((uint32_t)sx[j * 8 + c] << 3));
-                  st[c] = fmaf(d, (float)vv, st[c]);
+                  st[c] = fmaf(d * (float)vv, bi, st[c]);
                 } else {
-                  st[c] = fmaf(d, (float)vv, fmaf(mn, (float)sx[j * 8 + c], st[c]));
+                  st[c] = fmaf(fmaf(d, (float)vv, mn * (float)sx[j * 8 + c]), bi, st[c]);
                 }
               }
             }
           }
         }
 #pragma unroll
-        for (int c = 0; c < MC; ++c) acc[c] = fmaf(st[c], inv[c], acc[c]);
+        for (int c = 0; c < MC; ++c) acc[c] += st[c];
         __syncwarp();
         if (lane == 0) sm100::mbar_arrive(&dr_empty[di]);
       }
