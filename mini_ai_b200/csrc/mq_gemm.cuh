@@ -9,7 +9,8 @@
 //
 // Tile: 128 weight rows (MMA M, TMEM lanes) x BN activation rows (MMA N,
 // TMEM columns), K in steps of 64 (two quant blocks, one 128-byte swizzle
-// row of bf16). One CTA per tile, warp-specialised:
+// row of bf16). One CTA per tile, grid (activation tiles, weight tiles),
+// warp-specialised:
 //   warp 0      TMA loads of the x-split tiles (xh, xl) for each K step;
 //   warp 1      TMEM allocation and the single MMA-issuing thread;
 //   warps 2..5  load the packed weights, decode and scale each block in
@@ -141,7 +142,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kGemmRows, m0 = blockIdx.y * BN;
+  // Raster: the activation tile varies fastest, so the CTAs that share a
+  // weight tile run at the same time and its bytes come from HBM once.
+  const int n0 = blockIdx.y * kGemmRows, m0 = blockIdx.x * BN;
   const int KT = a.ktiles;
 
   if (threadIdx.x == 0) {

@@ -261,7 +261,7 @@ cudaError_t launch_gemm_t(const CUtensorMap &th, const CUtensorMap &tl, const Ge
   using L = GemmSmem<QT, BN, STAGES>;
   static std::atomic<uint64_t> smem_set{0};
   if (const cudaError_t e0 = raise_smem_limit(smem_set, gemm_kernel<QT, BN, STAGES>, L::kAlloc)) return e0;
-  const dim3 grid((a.w.rows + kGemmRows - 1) / kGemmRows, (a.m + BN - 1) / BN);
+  const dim3 grid((a.m + BN - 1) / BN, (a.w.rows + kGemmRows - 1) / kGemmRows);  // activation tile fastest
   gemm_kernel<QT, BN, STAGES><<<grid, kGemmThreads, L::kAlloc, s>>>(th, tl, a);
   count_launch();
   return cudaGetLastError();
