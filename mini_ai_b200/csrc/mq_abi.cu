@@ -137,6 +137,17 @@ int linear_dispatch(const mq_weight *w, const float *x, int m, int ldx, const fl
 }
 
 }  // namespace
+
+int run_linear_peer(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
+                    cudaStream_t s, const PeerOut &peer) {
+  if (g_path_mode != 0 || !gemm_supported(w->device) || m < 1 || m > decode_max_m() || m <= gemv_max_m())
+    return MQ_ERR_UNSUPPORTED;
+  if (m <= i8dec_max_m() && m <= 4) return run_i8dec(w, x, m, ldx, bias, y, ldy, s, nullptr, nullptr, &peer);
+  if (m > i8dec_max_m() && m <= 32 && w->foldable)
+    return run_tcdec(w, x, m, ldx, bias, y, ldy, s, nullptr, nullptr, true, &peer);
+  return MQ_ERR_UNSUPPORTED;
+}
+
 }  // namespace mq
 
 extern "C" {

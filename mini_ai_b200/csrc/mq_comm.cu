@@ -36,10 +36,12 @@
 #include <dlfcn.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
 #include "mq_common.cuh"
+#include "mq_peer.cuh"
 #include "mq_sm100.cuh"
 #include "mq_tcdec_api.h"
 
@@ -49,8 +51,6 @@ namespace mq {
 int gather_workspace_for(int device, cudaStream_t s, size_t bytes, void **out);
 void count_launch(int n);
 
-constexpr int kP2PMaxRanks = 8;
-constexpr size_t kP2PSlotFloats = size_t(1) << 20;  // 4 MiB per slot: m * rows_per_rank <= 1,048,576
 constexpr uint64_t kP2PWaitNs = 1000000000ull;  // default wait limit for a peer's arrival flag
 }  // namespace mq
 
@@ -115,10 +115,7 @@ __global__ void interleave_kernel(const float *__restrict__ g, int nranks, int m
   }
 }
 
-// Byte layout of a staging region: data [2][G][slot], flags [2][G] u32,
-// counters {epoch, push arrivals, pull arrivals, poisoned} u32.
-__host__ __device__ inline size_t p2p_data_bytes(int G) { return 2 * (size_t)G * kP2PSlotFloats * sizeof(float); }
-__host__ __device__ inline size_t p2p_region_bytes(int G) { return p2p_data_bytes(G) + (2 * (size_t)G + 4) * 4; }
+// Byte layout of a staging region: mq_peer.cuh.
 
 struct P2PArgs {
   float *y;          // the output [m, ldy]; this rank's slice at column rank * R
@@ -129,20 +126,6 @@ struct P2PArgs {
   uint64_t wait_ns;  // bound of the wait for a peer's flag
 };
 
-__device__ __forceinline__ uint32_t *p2p_flags(char *base, int G) {
-  return reinterpret_cast<uint32_t *>(base + p2p_data_bytes(G));
-}
-__device__ __forceinline__ float *p2p_slot(char *base, int G, int half, int src) {
-  return reinterpret_cast<float *>(base) + ((size_t)half * G + src) * kP2PSlotFloats;
-}
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 // This rank's slice [m, R] (row stride ldy) -> slot (half, rank) of every peer.
 template <bool VEC>
@@ -185,6 +168,9 @@ __global__ void __launch_bounds__(256) p2p_push_kernel(const P2PArgs a) {
 template <bool VEC>
 __global__ void __launch_bounds__(256) p2p_pull_kernel(const P2PArgs a) {
   __shared__ int s_ok;
+  // The previous kernel (push, or the decode kernel that pushed its slice
+  // itself) reads the epoch this kernel advances: it must have completed.
+  sm100::griddep_wait();
   char *mine = a.base[a.rank];
   uint32_t *flags = p2p_flags(mine, a.G);
   uint32_t *ctl = flags + 2 * a.G;
@@ -383,6 +369,24 @@ cudaError_t p2p_launch(const P2PArgs &a, int grid, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+// The pull alone: the decode kernel already stored this rank's slice into
+// the peers' staging and raised the flags.
+template <bool VEC>
+cudaError_t p2p_pull_launch(const P2PArgs &a, int grid, cudaStream_t s) {
+  p2p_pull_kernel<VEC><<<grid, 256, 0, s>>>(a);
+  count_launch(1);
+  return cudaGetLastError();
+}
+
+// MQ_P2P_FUSED=0 keeps the separate push kernel after the decode kernel.
+bool p2p_fused() {
+  static const bool on = [] {
+    const char *v = std::getenv("MQ_P2P_FUSED");
+    return !(v && *v && std::atoi(v) == 0);
+  }();
+  return on;
+}
+
 }  // namespace
 }  // namespace mq
 
@@ -496,13 +500,25 @@ int mq_linear_sharded_allgather(const mq_weight *w, const float *x, int m, int l
                   "peer-memory gather: a peer did not arrive within %llu ns in an earlier call on rank %d; this "
                   "communicator's gathers are disabled (destroy it and create a new one)",
                   (unsigned long long)comm->wait_ns, r);
-    int rc = mq_linear(w, x, m, ldx, bias_slice, y + (int64_t)r * R, ldy, stream);
-    if (rc) return rc;
     P2PArgs a{y, (int64_t)ldy, m, R, G, r, {}, comm->err_dev, comm->wait_ns};
     for (int p = 0; p < G; ++p) a.base[p] = comm->peer[p];
     const bool vec = R % 4 == 0 && ldy % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
     const int64_t n = (int64_t)m * R / (vec ? 4 : 1);
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148));
+    int rc = MQ_ERR_UNSUPPORTED;
+    if (p2p_fused()) {  // the decode kernel stores the slice into the peers itself: no push launch
+      PeerOut peer;
+      peer.G = G, peer.rank = r, peer.R = R;
+      for (int p = 0; p < G; ++p) peer.base[p] = comm->peer[p];
+      rc = run_linear_peer(w, x, m, ldx, bias_slice, y + (int64_t)r * R, ldy, s, peer);
+      if (rc == MQ_OK) {
+        e = vec ? p2p_pull_launch<true>(a, grid, s) : p2p_pull_launch<false>(a, grid, s);
+        return e == cudaSuccess ? MQ_OK : cuda_fail(e, "peer gather launch");
+      }
+      if (rc != MQ_ERR_UNSUPPORTED) return rc;
+    }
+    rc = mq_linear(w, x, m, ldx, bias_slice, y + (int64_t)r * R, ldy, stream);
+    if (rc) return rc;
     e = vec ? p2p_launch<true>(a, grid, s) : p2p_launch<false>(a, grid, s);
     return e == cudaSuccess ? MQ_OK : cuda_fail(e, "peer gather launch");
   }

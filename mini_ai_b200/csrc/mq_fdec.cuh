@@ -223,6 +223,7 @@ __global__ void __launch_bounds__(kFdThreads, 1)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::kNumBars);
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
   __shared__ int s_last;
+  __shared__ uint32_t s_peer_e;  // the gather's epoch, when the outputs also go to the peers
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = a.steps, T = a.tiles * a.steps, GR = gridDim.x, cta = blockIdx.x;
@@ -411,6 +412,8 @@ __global__ void __launch_bounds__(kFdThreads, 1)
     }
   } else {  // ------------------------------------------------ drainers (TMEM lane = tile row)
     sm100::griddep_wait();  // block sums, row scales, outputs and workspace
+    const uint32_t pe = a.peer.G > 1 ? peer_epoch(a.peer) : 0u;
+    if (warp == 12 && lane == 0) s_peer_e = pe;
     const int qq = warp & 3;
     const int r = 32 * qq + lane;
     const uint32_t lane_base = (uint32_t)(32 * qq) << 16;
@@ -430,9 +433,12 @@ __global__ void __launch_bounds__(kFdThreads, 1)
           const float bias = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
           for (int c = 0; c < NC; ++c)
-            if (c < a.m)
-              a.y[(int64_t)c * a.ldy + n] =
+            if (c < a.m) {
+              const float v =
                   EPI ? epilogue_out(acc[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n) : acc[c] + bias;
+              a.y[(int64_t)c * a.ldy + n] = v;
+              if (a.peer.G > 1) peer_store(a.peer, pe, c, n, v);
+            }
         }
         return;
       }
@@ -469,9 +475,12 @@ __global__ void __launch_bounds__(kFdThreads, 1)
           const float bias = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
           for (int c = 0; c < NC; ++c)
-            if (c < a.m)
-              a.y[(int64_t)c * a.ldy + n] =
+            if (c < a.m) {
+              const float v =
                   EPI ? epilogue_out(tot[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n) : tot[c] + bias;
+              a.y[(int64_t)c * a.ldy + n] = v;
+              if (a.peer.G > 1) peer_store(a.peer, pe, c, n, v);
+            }
         }
         if (warp == 12 && lane == 0) a.tickets[tile] = 0;  // ready for the next launch
       }
@@ -561,6 +570,7 @@ __global__ void __launch_bounds__(kFdThreads, 1)
 
   sm100::tc_fence_before();
   __syncthreads();
+  if (a.peer.G > 1) peer_finish(a.peer, s_peer_e);  // every CTA's outputs are in the peers' staging
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, 512);

@@ -27,6 +27,7 @@
 #include <climits>
 
 #include "mq_common.cuh"
+#include "mq_peer.cuh"
 #include "mq_sm100.cuh"
 
 namespace mq {
@@ -317,7 +318,8 @@ int run_sdec(const mq_weight *w, const float *x, int m, int64_t ldx, const float
              cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr);
 // folded: the scale-folded kernel (mq_fdec.cuh), for weights with mq_weight::foldable.
 int run_tcdec(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-              cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr, bool folded = false);
+              cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr, bool folded = false,
+              const PeerOut *peer = nullptr);
 int run_gemm(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
              cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr);
 

@@ -328,7 +328,7 @@ DecPlan tcdec_plan(const WeightView &w, int device, int max_grid) {
 
 int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const float *bias, float *y, int64_t ldy,
                  cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort, const float *gate,
-                 const float *resid, bool folded) {
+                 const float *resid, bool folded, const PeerOut *peer) {
   const int bn = folded ? fdec_tile_rows(mm) : dec_tile_rows(mm);
   if (folded)  // one scale per activation row: the folded kernel accumulates along K
     MQ_CUDA(launch_pdl(fold_prep_kernel, dim3(bn, (plan.steps + kFpSteps - 1) / kFpSteps), dim3(kFpThreads), 0, s,
@@ -343,6 +343,7 @@ int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const
     return rc;
   DecArgs a{w, mm, buf.xinv, buf.xsum, bias, y, ldy, buf.partial, buf.tickets, plan.steps, plan.tiles, buf.err,
             nan_on_abort, gate, resid};
+  if (peer) a.peer = *peer;
   cudaError_t e;
   if (folded) {
     switch (w.qtype) {
@@ -364,7 +365,8 @@ int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const
 // tcgen05 decode GEMM: up to 32 activation rows per launch (split + kernel);
 // `folded` runs the scale-folded kernel (mq_fdec.cuh), which needs a foldable weight.
 int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-              cudaStream_t s, const float *gate, const float *resid, bool folded) {
+              cudaStream_t s, const float *gate, const float *resid, bool folded, const PeerOut *peer) {
+  if (peer && m > 32) return fail(MQ_ERR_INVALID, "a fused gather needs one launch (m <= 32)");
   int *err_dev = nullptr, *err_host = nullptr;
   int rc = err_flag(wt->device, &err_dev, &err_host);
   if (rc) return rc;
@@ -395,7 +397,7 @@ int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
     buf.err = err_dev;
     if ((rc = tcdec_launch(w, x + (int64_t)i0 * ldx, mm, ldx, bias, y + (int64_t)i0 * ldy, ldy, s, plan, buf, 0,
                            gate ? gate + (int64_t)i0 * ldy : nullptr, resid ? resid + (int64_t)i0 * ldy : nullptr,
-                           folded)))
+                           folded, peer)))
       return rc;
   }
   return MQ_OK;
@@ -520,7 +522,9 @@ int i8dec_max_m() {
 
 // int8 tensor-core decode: up to 4 activation rows per launch.
 int run_i8dec(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-              cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr) {
+              cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr,
+              const PeerOut *peer = nullptr) {
+  if (peer && m > 4) return fail(MQ_ERR_INVALID, "a fused gather needs one launch (m <= 4)");
   int *err_dev = nullptr, *err_host = nullptr;
   int rc = err_flag(wt->device, &err_dev, &err_host);
   if (rc) return rc;
@@ -541,6 +545,7 @@ int run_i8dec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
     I8Args a{w, mm, x + (int64_t)i0 * ldx, ldx, bias, y + (int64_t)i0 * ldy, ldy, static_cast<float *>(ws), tickets,
              plan.steps, plan.tiles, err_dev, 0, gate ? gate + (int64_t)i0 * ldy : nullptr,
              resid ? resid + (int64_t)i0 * ldy : nullptr};
+    if (peer) a.peer = *peer;
     cudaError_t e;
     switch (w.qtype) {
     case MQ_Q8_0: e = launch_i8dec_q<MQ_Q8_0>(a, plan.grid, mc, s); break;

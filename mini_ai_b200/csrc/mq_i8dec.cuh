@@ -77,6 +77,7 @@
 #include <cuda_fp16.h>
 
 #include "mq_common.cuh"
+#include "mq_peer.cuh"
 #include "mq_sm100.cuh"
 #include "mq_tcdec.cuh"
 
@@ -113,6 +114,7 @@ struct I8Args {
   int nan_on_abort;
   const float *gate = nullptr;   // fused gate/up product: y = silu(gate) * (product + bias); gate [m, ldy]
   const float *resid = nullptr;  // residual add: y = resid + (product + bias); resid [m, ldy], may be y
+  PeerOut peer;                  // row-sharded linear: also store the outputs into the peers' staging (G > 1)
 };
 
 template <int QT, int MC>
@@ -243,6 +245,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::kNumBars);
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
   __shared__ int s_last;
+  __shared__ uint32_t s_peer_e;  // the gather's epoch, when the outputs also go to the peers
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = a.steps, T = a.tiles * a.steps, GR = gridDim.x, cta = blockIdx.x;
@@ -536,6 +539,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
     // group 0 adds them to its own (fixed order) and completes the tile.
     const int grp = warp > 20 ? 1 : 0;
     if (grp == 0) sm100::griddep_wait();  // outputs, partial slots and tickets may still be in use by the previous kernel
+    const uint32_t pe = (grp == 0 && a.peer.G > 1) ? peer_epoch(a.peer) : 0u;  // group 0 writes the outputs
+    if (warp == 16 && lane == 0) s_peer_e = pe;
     const int qq = warp & 3;
     const int r = 32 * qq + lane;
     const uint32_t lane_base = (uint32_t)(32 * qq) << 16;
@@ -559,7 +564,11 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
           const float bias = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
           for (int c = 0; c < MC; ++c)
-            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = EPI ? epilogue_out(acc[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n) : acc[c] + bias;
+            if (c < a.m) {
+              const float v = EPI ? epilogue_out(acc[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n) : acc[c] + bias;
+              a.y[(int64_t)c * a.ldy + n] = v;
+              if (a.peer.G > 1) peer_store(a.peer, pe, c, n, v);
+            }
         }
         return;
       }
@@ -587,7 +596,11 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
           const float bias = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
           for (int c = 0; c < MC; ++c)
-            if (c < a.m) a.y[(int64_t)c * a.ldy + n] = EPI ? epilogue_out(tot[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n) : tot[c] + bias;
+            if (c < a.m) {
+              const float v = EPI ? epilogue_out(tot[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n) : tot[c] + bias;
+              a.y[(int64_t)c * a.ldy + n] = v;
+              if (a.peer.G > 1) peer_store(a.peer, pe, c, n, v);
+            }
         }
         if (warp == 16 && lane == 0) a.tickets[tile] = 0;  // ready for the next launch
       }
@@ -703,6 +716,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
 
   sm100::tc_fence_before();
   __syncthreads();
+  if (a.peer.G > 1) peer_finish(a.peer, s_peer_e);  // every CTA's outputs are in the peers' staging
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, 512);

@@ -75,6 +75,7 @@
 #include <cuda_fp16.h>
 
 #include "mq_common.cuh"
+#include "mq_peer.cuh"
 #include "mq_sm100.cuh"
 #include "mq_tcdec_api.h"
 
@@ -103,6 +104,7 @@ struct DecArgs {
   int nan_on_abort;      // on a timed-out wait, write NaN outputs instead of skipping them
   const float *gate = nullptr;   // fused gate/up product: y = silu(gate) * (product + bias); gate [m, ldy]
   const float *resid = nullptr;  // residual add: y = resid + (product + bias); resid [m, ldy], may be y
+  PeerOut peer;                  // row-sharded linear: also store the outputs into the peers' staging (G > 1)
 };
 
 template <int QT, int BN>

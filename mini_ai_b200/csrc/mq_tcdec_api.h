@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include "mq_common.cuh"
+#include "mq_peer.cuh"
 
 namespace mq {
 
@@ -40,7 +41,17 @@ inline int fdec_tile_rows(int m) { return m <= 16 ? 16 : 32; }
 // from fdec_tile_rows), for weights whose scales allow the fold.
 int tcdec_launch(const WeightView &w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
                  cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort,
-                 const float *gate = nullptr, const float *resid = nullptr, bool folded = false);
+                 const float *gate = nullptr, const float *resid = nullptr, bool folded = false,
+                 const PeerOut *peer = nullptr);
+
+// The automatic decode kernel of mq_linear with the row-sharded gather fused
+// into its output stores (PeerOut, mq_peer.cuh): one launch that also stores
+// the slice into every peer's staging and raises the arrival flags. Returns
+// MQ_ERR_UNSUPPORTED (message unset) when the automatic choice for this
+// weight and m is not a single int8 or scale-folded decode launch, or a kernel
+// path is forced (mq_set_path); the caller then gathers separately.
+int run_linear_peer(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
+                    cudaStream_t s, const PeerOut &peer);
 
 bool gemm_supported(int device);
 
