@@ -20,7 +20,9 @@ the whole step.
   e2e   : through the public API with host buffers: every step copies every
           product's activations from pinned host memory (one host-to-device
           copy of the step's input arena) and every product's outputs back
-          (one device-to-host copy) inside the timed region.
+          (one device-to-host copy) inside the timed region; the copies run on
+          copy streams with double-buffered device arenas, overlapping the
+          next step's products, as a serving loop does.
 At one GPU the line also carries ``prefill``: the ragged prefill GEMM (Q8_0
 W 11008x4096 and 4096x11008, 8 requests of 1..512 rows packed to M = 1456)
 in TFLOP/s of 2*M*N*K against the measured dense bf16 peak, with its own
@@ -441,10 +443,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
 def _e2e(args, arm, torch, mq, comm, stream, dev, barrier, max_over_ranks) -> dict:
     """The same step end to end through the public API with host buffers (pinned),
-    on the caller's stream. Every product has its own input and output slice in
-    one pinned host arena and one device arena: a step copies all of its inputs
-    in with one host-to-device copy, runs the products through the Python API
-    and reads all of its results back with one device-to-host copy."""
+    as a serving loop runs it: every step copies all of its inputs from one
+    pinned host arena into a device arena (one host-to-device copy), runs the
+    products through the Python API on the caller's stream, and reads all of its
+    results back into a pinned host arena (one device-to-host copy). The copies
+    run on two copy streams and the device arenas are double-buffered, so step
+    s + 1's inputs come in and step s's outputs go out while the next products
+    compute; the timed region ends when the last step's results are on the
+    host."""
     prods = arm.prods
     x_off, y_off = [0], [0]
     for (_, m, _, n, k, _) in prods:
@@ -452,33 +458,61 @@ def _e2e(args, arm, torch, mq, comm, stream, dev, barrier, max_over_ranks) -> di
         y_off.append(y_off[-1] + m * n)
     hx_all = torch.empty(x_off[-1], dtype=torch.float32).pin_memory()
     hy_all = torch.empty(y_off[-1], dtype=torch.float32).pin_memory()
-    dx_all = torch.empty(x_off[-1], dtype=torch.float32, device=dev)
-    dy_all = torch.empty(y_off[-1], dtype=torch.float32, device=dev)
+    dx_all = [torch.empty(x_off[-1], dtype=torch.float32, device=dev) for _ in range(2)]
+    dy_all = [torch.empty(y_off[-1], dtype=torch.float32, device=dev) for _ in range(2)]
     for i, (_, m, _, n, k, _) in enumerate(prods):
         hx_all[x_off[i]:x_off[i + 1]].copy_(arm.xs[(m, k)].reshape(-1).cpu())
-    dxs = [dx_all[x_off[i]:x_off[i + 1]].view(m, k) for i, (_, m, _, n, k, _) in enumerate(prods)]
-    dys = [dy_all[y_off[i]:y_off[i + 1]].view(m, n) for i, (_, m, _, n, k, _) in enumerate(prods)]
+    dxs = [[dx_all[b][x_off[i]:x_off[i + 1]].view(m, k) for i, (_, m, _, n, k, _) in enumerate(prods)]
+           for b in range(2)]
+    dys = [[dy_all[b][y_off[i]:y_off[i + 1]].view(m, n) for i, (_, m, _, n, k, _) in enumerate(prods)]
+           for b in range(2)]
     apis = [mq.ShardedLinear.from_shard(h, comm) if arm.world > 1 else h for h in arm.handles]
+    h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    comp_done = [torch.cuda.Event() for _ in range(2)]
+    out_done = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        dx_all.copy_(hx_all, non_blocking=True)
+    def e2e_step(s):
+        b = s % 2
+        if s >= 2:
+            h2d.wait_event(comp_done[b])  # arena b's inputs were read by step s - 2
+        with torch.cuda.stream(h2d):
+            dx_all[b].copy_(hx_all, non_blocking=True)
+            in_ready[b].record(h2d)
+        stream.wait_event(in_ready[b])
+        if s >= 2:
+            stream.wait_event(out_done[b])  # arena b's outputs of step s - 2 are on the host
         for i in range(len(prods)):
-            apis[i].linear(dxs[i], out=dys[i], stream=stream)
-        hy_all.copy_(dy_all, non_blocking=True)
+            apis[i].linear(dxs[b][i], out=dys[b][i], stream=stream)
+        comp_done[b].record(stream)
+        d2h.wait_event(comp_done[b])
+        with torch.cuda.stream(d2h):
+            hy_all.copy_(dy_all[b], non_blocking=True)
+            out_done[b].record(d2h)
 
-    for _ in range(args.warmup):
-        e2e_step()
+    def run(steps):
+        start = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        h2d.wait_event(start)
+        for s in range(steps):
+            e2e_step(s)
+        stream.wait_event(out_done[(steps - 1) % 2])
+        end = torch.cuda.Event(enable_timing=True)
+        end.record(stream)
+        return start, end
+
+    run(args.warmup)
+    torch.cuda.synchronize(dev)
     barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record(stream)
+    e0, e1 = run(args.steps)
+    torch.cuda.synchronize(dev)
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     return {"value": round(work_rate(arm.wl, arm.work_per_step, e2e_ms / args.steps * 1e-3), 2),
             "unit": arm.wl["unit"], "h2d_bytes_per_step": 4 * x_off[-1], "d2h_bytes_per_step": 4 * y_off[-1],
-            "ms_per_step": round(e2e_ms / args.steps, 6)}
+            "ms_per_step": round(e2e_ms / args.steps, 6),
+            "copies": "double-buffered: step s + 1's inputs in and step s's outputs out on copy streams while "
+                      "the products compute"}
 
 
 FORWARD_EXE = ROOT / "mini_ai_b200" / "adapter" / "_ref" / "mini-ai-b200-forward"

@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(kFpThreads)
   }
 }
 
-template <int QT, int BN, int NC, bool EPI>
+template <int QT, int BN, int NC, bool EPI, bool PEER>
 __global__ void __launch_bounds__(kFdThreads, 1)
     fdec_kernel(const __grid_constant__ CUtensorMap tm_x, const DecArgs a) {
   using L = FdCfg<QT, BN>;
@@ -412,7 +412,7 @@ __global__ void __launch_bounds__(kFdThreads, 1)
     }
   } else {  // ------------------------------------------------ drainers (TMEM lane = tile row)
     sm100::griddep_wait();  // block sums, row scales, outputs and workspace
-    const uint32_t pe = a.peer.G > 1 ? peer_epoch(a.peer) : 0u;
+    const uint32_t pe = PEER ? peer_epoch(a.peer) : 0u;
     if (warp == 12 && lane == 0) s_peer_e = pe;
     const int qq = warp & 3;
     const int r = 32 * qq + lane;
@@ -437,7 +437,7 @@ __global__ void __launch_bounds__(kFdThreads, 1)
               const float v =
                   EPI ? epilogue_out(acc[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n) : acc[c] + bias;
               a.y[(int64_t)c * a.ldy + n] = v;
-              if (a.peer.G > 1) peer_store(a.peer, pe, c, n, v);
+              if constexpr (PEER) peer_store(a.peer, pe, c, n, v);
             }
         }
         return;
@@ -479,7 +479,7 @@ __global__ void __launch_bounds__(kFdThreads, 1)
               const float v =
                   EPI ? epilogue_out(tot[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n) : tot[c] + bias;
               a.y[(int64_t)c * a.ldy + n] = v;
-              if (a.peer.G > 1) peer_store(a.peer, pe, c, n, v);
+              if constexpr (PEER) peer_store(a.peer, pe, c, n, v);
             }
         }
         if (warp == 12 && lane == 0) a.tickets[tile] = 0;  // ready for the next launch
@@ -570,7 +570,7 @@ __global__ void __launch_bounds__(kFdThreads, 1)
 
   sm100::tc_fence_before();
   __syncthreads();
-  if (a.peer.G > 1) peer_finish(a.peer, s_peer_e);  // every CTA's outputs are in the peers' staging
+  if constexpr (PEER) peer_finish(a.peer, s_peer_e);  // every CTA's outputs are in the peers' staging
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, 512);

@@ -239,12 +239,13 @@ cudaError_t launch_tcdec_q(const CUtensorMap &tx, const DecArgs &a, int grid, in
   return launch_tcdec_t<QT, 32, 32, false>(tx, a, grid, s);
 }
 
-template <int QT, int BN, bool EPI>
+template <int QT, int BN, bool EPI, bool PEER = false>
 cudaError_t launch_fdec_t(const CUtensorMap &tx, const DecArgs &a, int grid, cudaStream_t s) {
   using L = FdCfg<QT, BN>;
   static std::atomic<uint64_t> smem_set{0};
-  if (const cudaError_t e0 = raise_smem_limit(smem_set, fdec_kernel<QT, BN, BN, EPI>, L::kAlloc)) return e0;
-  const cudaError_t e = launch_pdl(fdec_kernel<QT, BN, BN, EPI>, dim3(grid), dim3(kFdThreads), L::kAlloc, s, tx, a);
+  if (const cudaError_t e0 = raise_smem_limit(smem_set, fdec_kernel<QT, BN, BN, EPI, PEER>, L::kAlloc)) return e0;
+  const cudaError_t e =
+      launch_pdl(fdec_kernel<QT, BN, BN, EPI, PEER>, dim3(grid), dim3(kFdThreads), L::kAlloc, s, tx, a);
   count_launch();
   return e;
 }
@@ -252,6 +253,8 @@ cudaError_t launch_fdec_t(const CUtensorMap &tx, const DecArgs &a, int grid, cud
 template <int QT>
 cudaError_t launch_fdec_q(const CUtensorMap &tx, const DecArgs &a, int grid, int bn, cudaStream_t s) {
   const bool epi = a.gate || a.resid;
+  if (a.peer.G > 1)  // the row-sharded gather fused into the output stores (no epilogue there)
+    return bn == 16 ? launch_fdec_t<QT, 16, false, true>(tx, a, grid, s) : launch_fdec_t<QT, 32, false, true>(tx, a, grid, s);
   if (bn == 16) return epi ? launch_fdec_t<QT, 16, true>(tx, a, grid, s) : launch_fdec_t<QT, 16, false>(tx, a, grid, s);
   return epi ? launch_fdec_t<QT, 32, true>(tx, a, grid, s) : launch_fdec_t<QT, 32, false>(tx, a, grid, s);
 }
@@ -489,18 +492,23 @@ int run_sdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const floa
 
 namespace {
 
-template <int QT, int MC, bool EPI>
+template <int QT, int MC, bool EPI, bool PEER = false>
 cudaError_t launch_i8dec_t(const I8Args &a, int grid, cudaStream_t s) {
   using L = I8Cfg<QT, MC>;
   static std::atomic<uint64_t> smem_set{0};
-  if (const cudaError_t e0 = raise_smem_limit(smem_set, i8dec_kernel<QT, MC, EPI>, L::kAlloc)) return e0;
-  const cudaError_t e = launch_pdl(i8dec_kernel<QT, MC, EPI>, dim3(grid), dim3(kI8Threads), L::kAlloc, s, a);
+  if (const cudaError_t e0 = raise_smem_limit(smem_set, i8dec_kernel<QT, MC, EPI, PEER>, L::kAlloc)) return e0;
+  const cudaError_t e = launch_pdl(i8dec_kernel<QT, MC, EPI, PEER>, dim3(grid), dim3(kI8Threads), L::kAlloc, s, a);
   count_launch();
   return e;
 }
 
 template <int QT>
 cudaError_t launch_i8dec_q(const I8Args &a, int grid, int mc, cudaStream_t s) {
+  if (a.peer.G > 1) {  // the row-sharded gather fused into the output stores (no epilogue there)
+    if (mc == 1) return launch_i8dec_t<QT, 1, false, true>(a, grid, s);
+    if (mc == 2) return launch_i8dec_t<QT, 2, false, true>(a, grid, s);
+    return launch_i8dec_t<QT, 4, false, true>(a, grid, s);
+  }
   if (a.gate || a.resid) {
     if (mc == 1) return launch_i8dec_t<QT, 1, true>(a, grid, s);
     if (mc == 2) return launch_i8dec_t<QT, 2, true>(a, grid, s);

@@ -230,7 +230,7 @@ __host__ __device__ inline int i8_slot_elem(int qtype, int c, int p) {
 
 // EPI: the output write applies the epilogues of I8Args::gate / resid (a separate
 // instantiation: the plain product is compiled without them).
-template <int QT, int MC, bool EPI>
+template <int QT, int MC, bool EPI, bool PEER>
 __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
   using L = I8Cfg<QT, MC>;
   constexpr int PS = L::PS, NB = L::NB, DS = L::DS, NA = L::NA, ND = L::ND, NCOL = L::NCOL, BB = L::BB;
@@ -539,7 +539,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
     // group 0 adds them to its own (fixed order) and completes the tile.
     const int grp = warp > 20 ? 1 : 0;
     if (grp == 0) sm100::griddep_wait();  // outputs, partial slots and tickets may still be in use by the previous kernel
-    const uint32_t pe = (grp == 0 && a.peer.G > 1) ? peer_epoch(a.peer) : 0u;  // group 0 writes the outputs
+    const uint32_t pe = (PEER && grp == 0) ? peer_epoch(a.peer) : 0u;  // group 0 writes the outputs
     if (warp == 16 && lane == 0) s_peer_e = pe;
     const int qq = warp & 3;
     const int r = 32 * qq + lane;
@@ -567,7 +567,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
             if (c < a.m) {
               const float v = EPI ? epilogue_out(acc[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n) : acc[c] + bias;
               a.y[(int64_t)c * a.ldy + n] = v;
-              if (a.peer.G > 1) peer_store(a.peer, pe, c, n, v);
+              if constexpr (PEER) peer_store(a.peer, pe, c, n, v);
             }
         }
         return;
@@ -599,7 +599,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
             if (c < a.m) {
               const float v = EPI ? epilogue_out(tot[c] + bias, a.gate, a.resid, (int64_t)c * a.ldy + n) : tot[c] + bias;
               a.y[(int64_t)c * a.ldy + n] = v;
-              if (a.peer.G > 1) peer_store(a.peer, pe, c, n, v);
+              if constexpr (PEER) peer_store(a.peer, pe, c, n, v);
             }
         }
         if (warp == 16 && lane == 0) a.tickets[tile] = 0;  // ready for the next launch
@@ -716,7 +716,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) i8dec_kernel(const I8Args a) {
 
   sm100::tc_fence_before();
   __syncthreads();
-  if (a.peer.G > 1) peer_finish(a.peer, s_peer_e);  // every CTA's outputs are in the peers' staging
+  if constexpr (PEER) peer_finish(a.peer, s_peer_e);  // every CTA's outputs are in the peers' staging
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem, 512);
