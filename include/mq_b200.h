@@ -218,7 +218,10 @@ int mq_linear_sharded_allgather(const mq_weight *shard, const float *x, int m, i
  * 3 = force the tcgen05 int8 decode GEMV, 4 = force the tcgen05 fp16 decode
  * GEMM, 5 = force the SIMT dp4a decode GEMV, 6 = force the tcgen05
  * scale-folded decode GEMM (MQ_ERR_UNSUPPORTED for weights outside its
- * range); other values are ignored. Returns the previous mode. */
+ * range), 7 = force the scale-folded decode GEMM on CTA pairs (tcgen05
+ * cta_group::2; MQ_ERR_UNSUPPORTED for weights outside the fold's range or
+ * with an odd number of 128-row tiles); other values are ignored. Returns the
+ * previous mode. */
 int mq_set_path(int mode);
 
 /* Number of kernels this library has launched in this process (all devices,

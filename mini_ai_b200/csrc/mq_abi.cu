@@ -125,6 +125,13 @@ int linear_dispatch(const mq_weight *w, const float *x, int m, int ldx, const fl
   if (mode == 3) return run_i8dec(w, x, m, ldx, bias, y, ldy, s, gate, resid);
   if (mode == 4) return run_tcdec(w, x, m, ldx, bias, y, ldy, s, gate, resid);
   if (mode == 5) return run_gemv(w, x, m, ldx, bias, y, ldy, s, gate, resid);
+  if (mode == 7) {
+    if (!w->foldable)
+      return fail(MQ_ERR_UNSUPPORTED, "a block scale of this weight is too large for the scale-folded decode kernel");
+    if (w->v.tiles % 2 != 0)
+      return fail(MQ_ERR_UNSUPPORTED, "the CTA-pair decode kernel needs an even number of 128-row tiles");
+    return run_tcdec(w, x, m, ldx, bias, y, ldy, s, gate, resid, true, nullptr, true);
+  }
   if (mode == 6) {
     if (!w->foldable)
       return fail(MQ_ERR_UNSUPPORTED, "a block scale of this weight is too large for the scale-folded decode kernel");
@@ -339,7 +346,7 @@ int mq_weight_export(const mq_weight *w, void *dst, size_t dst_bytes) {
 
 int mq_set_path(int mode) {
   const int prev = g_path_mode;
-  if (mode >= 0 && mode <= 6) g_path_mode = mode;
+  if (mode >= 0 && mode <= 7) g_path_mode = mode;
   return prev;
 }
 

@@ -319,7 +319,7 @@ int run_sdec(const mq_weight *w, const float *x, int m, int64_t ldx, const float
 // folded: the scale-folded kernel (mq_fdec.cuh), for weights with mq_weight::foldable.
 int run_tcdec(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
               cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr, bool folded = false,
-              const PeerOut *peer = nullptr);
+              const PeerOut *peer = nullptr, bool pairs = false);
 int run_gemm(const mq_weight *w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
              cudaStream_t s, const float *gate = nullptr, const float *resid = nullptr);
 

@@ -10,6 +10,7 @@
 #include <utility>
 
 #include "mq_fdec.cuh"
+#include "mq_fdec2.cuh"
 #include "mq_gemm.cuh"
 #include "mq_gemv.cuh"
 #include "mq_i8dec.cuh"
@@ -17,6 +18,8 @@
 #include "mq_tcdec.cuh"
 
 namespace mq {
+
+int env_threshold(const char *name, int dflt);  // integer from the environment, or dflt
 
 namespace {
 
@@ -250,6 +253,40 @@ cudaError_t launch_fdec_t(const CUtensorMap &tx, const DecArgs &a, int grid, cud
   return e;
 }
 
+// The CTA-pair form: clusters of 2 CTAs, launched with programmatic stream
+// serialization like the others (grid even).
+template <int QT, int BN, bool EPI>
+cudaError_t launch_fdec2_t(const CUtensorMap &tx, const DecArgs &a, int grid, cudaStream_t s) {
+  using L = Fd2Cfg<QT, BN>;
+  static std::atomic<uint64_t> smem_set{0};
+  if (const cudaError_t e0 = raise_smem_limit(smem_set, fdec2_kernel<QT, BN, BN, EPI>, L::kAlloc)) return e0;
+  static const bool pdl = env_threshold("MQ_PDL", 1) != 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kFdThreads);
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, fdec2_kernel<QT, BN, BN, EPI>, tx, a);
+  count_launch();
+  return e;
+}
+
+template <int QT>
+cudaError_t launch_fdec2_q(const CUtensorMap &tx, const DecArgs &a, int grid, int bn, cudaStream_t s) {
+  const bool epi = a.gate || a.resid;
+  if (bn == 16) return epi ? launch_fdec2_t<QT, 16, true>(tx, a, grid, s) : launch_fdec2_t<QT, 16, false>(tx, a, grid, s);
+  return epi ? launch_fdec2_t<QT, 32, true>(tx, a, grid, s) : launch_fdec2_t<QT, 32, false>(tx, a, grid, s);
+}
+
 template <int QT>
 cudaError_t launch_fdec_q(const CUtensorMap &tx, const DecArgs &a, int grid, int bn, cudaStream_t s) {
   const bool epi = a.gate || a.resid;
@@ -331,7 +368,7 @@ DecPlan tcdec_plan(const WeightView &w, int device, int max_grid) {
 
 int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const float *bias, float *y, int64_t ldy,
                  cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort, const float *gate,
-                 const float *resid, bool folded, const PeerOut *peer) {
+                 const float *resid, bool folded, const PeerOut *peer, bool pairs_wanted) {
   const int bn = folded ? fdec_tile_rows(mm) : dec_tile_rows(mm);
   if (folded)  // one scale per activation row: the folded kernel accumulates along K
     MQ_CUDA(launch_pdl(fold_prep_kernel, dim3(bn, (plan.steps + kFpSteps - 1) / kFpSteps), dim3(kFpThreads), 0, s,
@@ -340,15 +377,27 @@ int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const
     MQ_CUDA(launch_pdl(dec_prep_kernel, dim3(plan.steps, (bn + 7) / 8), dim3(256), 0, s, x, ldx, mm, w.cols,
                        plan.kpad, bn, buf.x2, buf.xsum, buf.xinv, (int)(w.qtype == MQ_Q4_1)));
   count_launch();
+  // The scale-folded kernel on CTA pairs (mq_fdec2.cuh), when asked for and
+  // the weight has an even number of tiles; each CTA of a pair loads bn
+  // activation rows.
+  const bool pairs = folded && pairs_wanted && !peer && w.tiles % 2 == 0 && plan.grid >= 2;
   CUtensorMap tx;
   int rc;
-  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf.x2, 2 * bn, plan.kpad, plan.kpad, 64, 2 * bn)))
+  if ((rc = make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf.x2, 2 * bn, plan.kpad, plan.kpad, 64,
+                      pairs ? bn : 2 * bn)))
     return rc;
   DecArgs a{w, mm, buf.xinv, buf.xsum, bias, y, ldy, buf.partial, buf.tickets, plan.steps, plan.tiles, buf.err,
             nan_on_abort, gate, resid};
   if (peer) a.peer = *peer;
   cudaError_t e;
-  if (folded) {
+  if (pairs) {
+    const int grid = std::min(plan.grid, (w.tiles / 2) * plan.steps * 2) & ~1;
+    switch (w.qtype) {
+    case MQ_Q8_0: e = launch_fdec2_q<MQ_Q8_0>(tx, a, grid, bn, s); break;
+    case MQ_Q4_0: e = launch_fdec2_q<MQ_Q4_0>(tx, a, grid, bn, s); break;
+    default: e = launch_fdec2_q<MQ_Q4_1>(tx, a, grid, bn, s); break;
+    }
+  } else if (folded) {
     switch (w.qtype) {
     case MQ_Q8_0: e = launch_fdec_q<MQ_Q8_0>(tx, a, plan.grid, bn, s); break;
     case MQ_Q4_0: e = launch_fdec_q<MQ_Q4_0>(tx, a, plan.grid, bn, s); break;
@@ -368,7 +417,8 @@ int tcdec_launch(const WeightView &w, const float *x, int mm, int64_t ldx, const
 // tcgen05 decode GEMM: up to 32 activation rows per launch (split + kernel);
 // `folded` runs the scale-folded kernel (mq_fdec.cuh), which needs a foldable weight.
 int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
-              cudaStream_t s, const float *gate, const float *resid, bool folded, const PeerOut *peer) {
+              cudaStream_t s, const float *gate, const float *resid, bool folded, const PeerOut *peer,
+              bool pairs) {
   if (peer && m > 32) return fail(MQ_ERR_INVALID, "a fused gather needs one launch (m <= 32)");
   int *err_dev = nullptr, *err_host = nullptr;
   int rc = err_flag(wt->device, &err_dev, &err_host);
@@ -400,7 +450,7 @@ int run_tcdec(const mq_weight *wt, const float *x, int m, int64_t ldx, const flo
     buf.err = err_dev;
     if ((rc = tcdec_launch(w, x + (int64_t)i0 * ldx, mm, ldx, bias, y + (int64_t)i0 * ldy, ldy, s, plan, buf, 0,
                            gate ? gate + (int64_t)i0 * ldy : nullptr, resid ? resid + (int64_t)i0 * ldy : nullptr,
-                           folded, peer)))
+                           folded, peer, pairs)))
       return rc;
   }
   return MQ_OK;

@@ -42,7 +42,7 @@ inline int fdec_tile_rows(int m) { return m <= 16 ? 16 : 32; }
 int tcdec_launch(const WeightView &w, const float *x, int m, int64_t ldx, const float *bias, float *y, int64_t ldy,
                  cudaStream_t s, const DecPlan &plan, const DecBuffers &buf, int nan_on_abort,
                  const float *gate = nullptr, const float *resid = nullptr, bool folded = false,
-                 const PeerOut *peer = nullptr);
+                 const PeerOut *peer = nullptr, bool pairs = false);
 
 // The automatic decode kernel of mq_linear with the row-sharded gather fused
 // into its output stores (PeerOut, mq_peer.cuh): one launch that also stores

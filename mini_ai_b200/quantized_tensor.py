@@ -281,7 +281,7 @@ def CudaDeviceInfo() -> str:
 def set_path(mode: int) -> int:
     """Kernel selection for this thread (mq_set_path): 0 automatic, 1 stream-K SIMT GEMV,
     2 tcgen05 prefill GEMM, 3 tcgen05 int8 decode GEMV, 4 tcgen05 fp16 decode GEMM,
-    5 SIMT dp4a decode GEMV, 6 tcgen05 scale-folded decode GEMM."""
+    5 SIMT dp4a decode GEMV, 6 tcgen05 scale-folded decode GEMM, 7 the same on CTA pairs (cta_group::2)."""
     return lib().mq_set_path(mode)
 
 

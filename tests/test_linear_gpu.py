@@ -210,7 +210,13 @@ def test_dimension_mismatch_raises(mq, cuda_device):
 
 
 PATHS = {1: "streamk_simt_gemv", 3: "tcgen05_i8_decode", 4: "tcgen05_decode", 2: "tcgen05_gemm", 5: "simt_dp4a_gemv",
-         6: "tcgen05_folded_decode"}
+         6: "tcgen05_folded_decode", 7: "tcgen05_folded_decode_cta_pairs"}
+
+
+def _rows(path, rows):
+    """The CTA-pair kernel (path 7) takes weights with an even number of 128-row
+    tiles: 300 rows (3 tiles) become 200 (2 tiles, still a row tail)."""
+    return 200 if path == 7 and rows == 300 else rows
 
 
 @pytest.mark.parametrize("path", sorted(PATHS), ids=lambda p: PATHS[p])
@@ -219,8 +225,9 @@ def test_every_path_against_oracle(mq, oracle, cuda_device, path, q):
     """Each kernel, forced, on odd shapes: tail blocks (K % 32), row tails
     (N % 16, N % 128), activation counts around every tile edge."""
     ms = {1: [1, 2, 3, 4, 5, 9], 3: [1, 2, 3, 4, 5, 9], 4: [1, 2, 4, 5, 8, 9, 16, 17, 32, 33],
-          2: [1, 7, 128, 129, 300], 5: [1, 2, 3, 5], 6: [1, 5, 8, 9, 16, 17, 32, 33]}[path]
-    for rows, cols in [(300, 4097), (136, 320), (1000, 96)]:
+          2: [1, 7, 128, 129, 300], 5: [1, 2, 3, 5], 6: [1, 5, 8, 9, 16, 17, 32, 33],
+          7: [1, 5, 8, 9, 16, 17, 32, 33]}[path]
+    for rows, cols in [(_rows(path, 300), 4097), (136, 320), (1000, 96)]:
         for m in ms:
             s, x, y_ref, bound = _llama_case(mq, oracle, q, rows, cols, m, seed=rows * 7 + m + path)
             assert_linear_close(gpu_linear(mq, s, x, cuda_device, path=path), y_ref, bound)
@@ -261,8 +268,8 @@ def test_swiglu_gate_up_against_oracle(mq, oracle, cuda_device, path, q):
     Tolerance: the linear parity bound carried through silu (|silu'| < 1.1)."""
     torch = _torch()
     ms = {0: [1, 3, 16, 40], 1: [1, 3, 5], 3: [1, 2, 4, 5], 4: [1, 5, 16, 33], 2: [1, 129], 5: [1, 2, 3],
-          6: [5, 16, 32]}[path]
-    for rows, cols in [(300, 4097), (1024, 4096)]:
+          6: [5, 16, 32], 7: [5, 16, 32]}[path]
+    for rows, cols in [(_rows(path, 300), 4097), (1024, 4096)]:
         for m in ms:
             sg, x, g_ref, bg = _llama_case(mq, oracle, q, rows, cols, m, seed=rows * 3 + m + path * 11)
             su, _, _, _ = _llama_case(mq, oracle, q, rows, cols, m, seed=rows * 5 + m + path * 13)
@@ -310,8 +317,8 @@ def test_residual_add_against_oracle(mq, oracle, cuda_device, path, q):
     within the parity bound of the oracle, and bit-identical to the unfused product plus the add."""
     torch = _torch()
     ms = {0: [1, 3, 16, 40], 1: [1, 3, 5], 3: [1, 2, 4, 5], 4: [1, 5, 16, 33], 2: [1, 129], 5: [1, 2, 3],
-          6: [5, 16, 32]}[path]
-    for rows, cols in [(300, 4097), (1024, 4096)]:
+          6: [5, 16, 32], 7: [5, 16, 32]}[path]
+    for rows, cols in [(_rows(path, 300), 4097), (1024, 4096)]:
         for m in ms:
             s, x, y_ref, bound = _llama_case(mq, oracle, q, rows, cols, m, seed=rows * 17 + m + path * 7)
             rng = np.random.default_rng(rows + m)
@@ -358,4 +365,23 @@ def test_large_scales_fall_back_from_the_folded_kernel(mq, oracle, cuda_device):
     finally:
         mq.set_path(prev)
     torch.cuda.synchronize(cuda_device)
+    dw.close()
+
+
+def test_cta_pair_kernel_rejects_odd_tile_counts(mq, cuda_device):
+    """The CTA-pair kernel processes two 128-row tiles per pair: a weight with
+    an odd number of tiles is refused when that kernel is forced, and the
+    automatic path serves it."""
+    torch = _torch()
+    rng = np.random.default_rng(7)
+    s = mq.QuantizeTensor((rng.standard_normal((300, 256)) * 0.02).astype(np.float32), Q4_0)  # 3 tiles
+    dw = mq.CudaWeight(s, device=cuda_device)
+    x = dev(rng.standard_normal((8, 256)).astype(np.float32), cuda_device)
+    prev = mq.set_path(7)
+    try:
+        with pytest.raises(mq.MQError, match="even number of 128-row tiles"):
+            dw.linear(x)
+    finally:
+        mq.set_path(prev)
+    assert torch.isfinite(dw.linear(x)).all()
     dw.close()

@@ -132,13 +132,15 @@ def _outlier_case(q, rows, cols, m, seed):
 
 
 # Paths (mq_set_path): 0 automatic, 1 stream-K SIMT GEMV, 3 tcgen05 int8 decode, 4 tcgen05 fp16 decode,
-# 5 SIMT dp4a GEMV, 6 tcgen05 scale-folded decode.
-OUTLIER_PATHS = {0: [1, 2, 4, 16, 32], 1: [1, 2, 4], 3: [1, 2, 3, 4], 4: [1, 5, 16, 32], 5: [1, 2, 3], 6: [5, 16, 32]}
+# 5 SIMT dp4a GEMV, 6 tcgen05 scale-folded decode, 7 the same on CTA pairs.
+OUTLIER_PATHS = {0: [1, 2, 4, 16, 32], 1: [1, 2, 4], 3: [1, 2, 3, 4], 4: [1, 5, 16, 32], 5: [1, 2, 3], 6: [5, 16, 32],
+                 7: [5, 16, 32]}
 
 
 @pytest.mark.parametrize("path", sorted(OUTLIER_PATHS), ids=lambda p: {0: "automatic", 1: "streamk_simt_gemv",
                                                                       3: "tcgen05_i8_decode", 4: "tcgen05_decode",
-                                                                      5: "simt_dp4a_gemv", 6: "tcgen05_folded_decode"}[p])
+                                                                      5: "simt_dp4a_gemv", 6: "tcgen05_folded_decode",
+                                                                      7: "tcgen05_folded_decode_cta_pairs"}[p])
 @pytest.mark.parametrize("q", QTYPES, ids=lambda q: NAMES[q])
 def test_activation_outliers(mq, oracle, cuda_device, path, q):
     torch = _torch()
