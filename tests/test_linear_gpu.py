@@ -385,3 +385,25 @@ def test_cta_pair_kernel_rejects_odd_tile_counts(mq, cuda_device):
         mq.set_path(prev)
     assert torch.isfinite(dw.linear(x)).all()
     dw.close()
+
+
+def test_two_devices_one_process(mq, oracle):
+    """One process drives two GPUs: every kernel class's first launch on the
+    second device raises its shared-memory limit there (the attribute is per
+    device), and both devices give bit-identical results within the oracle's
+    bound."""
+    torch = _torch()
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    rows, cols = 1024, 4096
+    for q in QTYPES:
+        for m in (1, 4, 16, 32, 64):  # int8 decode, folded decode, prefill GEMM
+            s, x, y_ref, bound = _llama_case(mq, oracle, q, rows, cols, m, seed=q * 101 + m)
+            ys = []
+            for d in (1, 0):  # device 1 first: its first launches set that device's limits
+                w = mq.CudaWeight(s, device=d)
+                with torch.cuda.device(d):
+                    ys.append(w.linear(dev(x, d)).cpu().numpy())
+                w.close()
+            assert np.array_equal(ys[0], ys[1])
+            assert_linear_close(ys[0], y_ref, bound)
