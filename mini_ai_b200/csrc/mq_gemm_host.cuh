@@ -296,13 +296,28 @@ cudaError_t launch_fdec_q(const CUtensorMap &tx, const DecArgs &a, int grid, int
   return epi ? launch_fdec_t<QT, 32, true>(tx, a, grid, s) : launch_fdec_t<QT, 32, false>(tx, a, grid, s);
 }
 
-template <int QT, int BN, int STAGES>
-cudaError_t launch_gemm_t(const CUtensorMap &th, const CUtensorMap &tl, const GemmArgs &a, cudaStream_t s) {
+// Schedule of the persistent GEMM (one CTA per SM): whole waves of tiles,
+// then the tail tiles split into K pieces of at least kGemmMinSteps steps so
+// that the tail takes about one piece's time.
+constexpr int kGemmMinSteps = 8;
+template <int BN>
+void gemm_schedule(GemmArgs &a, int sms, int *grid) {
+  const int tiles = ((a.m + BN - 1) / BN) * ((a.w.rows + kGemmRows - 1) / kGemmRows);
+  a.waves = tiles / sms;
+  a.tail = tiles % sms;
+  a.split = a.tail ? std::max(1, std::min(sms / a.tail, a.ktiles / kGemmMinSteps)) : 1;
+  *grid = a.waves ? sms : a.tail * a.split;
+}
+
+template <int QT, int BN, int STAGES, bool FOLD>
+cudaError_t launch_gemm_t(const CUtensorMap &th, const CUtensorMap &tl, const GemmArgs &a, int sms, cudaStream_t s) {
   using L = GemmSmem<QT, BN, STAGES>;
   static std::atomic<uint64_t> smem_set{0};
-  if (const cudaError_t e0 = raise_smem_limit(smem_set, gemm_kernel<QT, BN, STAGES>, L::kAlloc)) return e0;
-  const dim3 grid((a.m + BN - 1) / BN, (a.w.rows + kGemmRows - 1) / kGemmRows);  // activation tile fastest
-  gemm_kernel<QT, BN, STAGES><<<grid, kGemmThreads, L::kAlloc, s>>>(th, tl, a);
+  if (const cudaError_t e0 = raise_smem_limit(smem_set, gemm_kernel<QT, BN, STAGES, FOLD>, L::kAlloc)) return e0;
+  GemmArgs b = a;
+  int grid = 1;
+  gemm_schedule<BN>(b, sms, &grid);
+  gemm_kernel<QT, BN, STAGES, FOLD><<<grid, kGemmThreads, L::kAlloc, s>>>(th, tl, b);
   count_launch();
   return cudaGetLastError();
 }
@@ -686,27 +701,54 @@ int run_gemm(const mq_weight *wt, const float *x, int m, int64_t ldx, const floa
   }
   const WeightView &w = wt->v;
   const int kpad = w.nb * 32;
-  const size_t half = (size_t)m * kpad * sizeof(__nv_bfloat16);
+  constexpr int BN = 256, STAGES = 2;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, wt->device);
+  const int ktiles = (w.nb + 1) / 2;
+  const int tiles = ((m + BN - 1) / BN) * ((w.rows + kGemmRows - 1) / kGemmRows);
+  int *tickets = nullptr;
+  if ((rc = tickets_for(wt->device, s, (size_t)tiles, &tickets))) return rc;
+  // The scale-folded form for weights whose every d * code fits fp16 (Q4_1's
+  // block minimum has no exact fold); MQ_GEMM_FOLD=0 keeps the bf16 form.
+  static const bool fold_on = env_threshold("MQ_GEMM_FOLD", 1) != 0;
+  const bool fold = fold_on && wt->foldable && w.qtype != MQ_Q4_1;
+  const size_t half = ((size_t)m * kpad * 2 + 255) & ~size_t(255);  // bf16 or fp16 [m, kpad]
+  const size_t pbytes = (size_t)sms * BN * kGemmRows * sizeof(float);  // split pieces' partial tiles, one per CTA
+  const size_t ibytes = ((size_t)m * sizeof(float) + 255) & ~size_t(255);
   void *ws = nullptr;
-  rc = workspace_for(wt->device, s, 2 * half, &ws);
+  rc = workspace_for(wt->device, s, 2 * half + pbytes + ibytes, &ws);
   if (rc) return rc;
-  __nv_bfloat16 *xh = static_cast<__nv_bfloat16 *>(ws);
-  __nv_bfloat16 *xl = reinterpret_cast<__nv_bfloat16 *>(static_cast<uint8_t *>(ws) + half);
-  const int64_t pairs = (int64_t)m * (kpad / 2);
-  split_x_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, s>>>(x, ldx, m, w.cols, kpad, xh, xl);
+  uint8_t *xh = static_cast<uint8_t *>(ws), *xl = xh + half;
+  float *part = reinterpret_cast<float *>(xh + 2 * half);
+  float *xinv = reinterpret_cast<float *>(xh + 2 * half + pbytes);
+  if (fold) {
+    split_x_f16_kernel<<<(unsigned)m, kSplitThreads, 0, s>>>(x, ldx, w.cols, kpad, reinterpret_cast<__half *>(xh),
+                                                             reinterpret_cast<__half *>(xl), xinv);
+  } else {
+    const int64_t pairs = (int64_t)m * (kpad / 2);
+    split_x_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, s>>>(x, ldx, m, w.cols, kpad,
+                                                                   reinterpret_cast<__nv_bfloat16 *>(xh),
+                                                                   reinterpret_cast<__nv_bfloat16 *>(xl));
+  }
   count_launch();
   MQ_CUDA(cudaGetLastError());
 
-  constexpr int BN = 256, STAGES = 2;
-  CUtensorMap th, tl;
+  CUtensorMap th, tl;  // 2-byte elements, bf16 or fp16 alike (the copies are bitwise; out of range reads zero)
   if ((rc = make_tmap_bf16(&th, xh, m, kpad, BN))) return rc;
   if ((rc = make_tmap_bf16(&tl, xl, m, kpad, BN))) return rc;
-  GemmArgs a{w, y, ldy, bias, m, (w.nb + 1) / 2, err_dev, gate, resid};
+  GemmArgs a{w, y, ldy, bias, m, ktiles, err_dev, gate, resid, tickets, part};
+  a.xinv = xinv;
   cudaError_t e;
   switch (w.qtype) {
-  case MQ_Q8_0: e = launch_gemm_t<MQ_Q8_0, BN, STAGES>(th, tl, a, s); break;
-  case MQ_Q4_0: e = launch_gemm_t<MQ_Q4_0, BN, STAGES>(th, tl, a, s); break;
-  default: e = launch_gemm_t<MQ_Q4_1, BN, STAGES>(th, tl, a, s); break;
+  case MQ_Q8_0:
+    e = fold ? launch_gemm_t<MQ_Q8_0, BN, STAGES, true>(th, tl, a, sms, s)
+             : launch_gemm_t<MQ_Q8_0, BN, STAGES, false>(th, tl, a, sms, s);
+    break;
+  case MQ_Q4_0:
+    e = fold ? launch_gemm_t<MQ_Q4_0, BN, STAGES, true>(th, tl, a, sms, s)
+             : launch_gemm_t<MQ_Q4_0, BN, STAGES, false>(th, tl, a, sms, s);
+    break;
+  default: e = launch_gemm_t<MQ_Q4_1, BN, STAGES, false>(th, tl, a, sms, s); break;
   }
   if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
   return MQ_OK;

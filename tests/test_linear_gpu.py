@@ -357,6 +357,11 @@ def test_large_scales_fall_back_from_the_folded_kernel(mq, oracle, cuda_device):
     y_ref = oracle.linear(Q8_0, s.bytes, rows, cols, x, threads=THREADS)
     bound = abs_dot_bound(oracle.dequantize(Q8_0, s.bytes, rows, cols), x)
     assert_linear_close(gpu_linear(mq, s, x, cuda_device, path=0), y_ref, bound)
+    # Prefill rows: the GEMM keeps such a weight on its bf16 form.
+    xg = rng.standard_normal((64, cols)).astype(np.float32)
+    bound_g = abs_dot_bound(oracle.dequantize(Q8_0, s.bytes, rows, cols), xg)
+    assert_linear_close(gpu_linear(mq, s, xg, cuda_device, path=0),
+                        oracle.linear(Q8_0, s.bytes, rows, cols, xg, threads=THREADS), bound_g)
     dw = mq.CudaWeight(s, device=cuda_device)
     prev = mq.set_path(6)
     try:
@@ -366,6 +371,27 @@ def test_large_scales_fall_back_from_the_folded_kernel(mq, oracle, cuda_device):
         mq.set_path(prev)
     torch.cuda.synchronize(cuda_device)
     dw.close()
+
+
+@pytest.mark.parametrize("q", [Q8_0, Q4_0, Q4_1], ids=["q8_0", "q4_0", "q4_1"])
+def test_gemm_rows_of_any_magnitude(mq, oracle, cuda_device, q):
+    """Prefill GEMM (m > 32) with activation rows from 1e-30 to 1e30 in one
+    launch, an all-zero row and a row with one large outlier: the scale-folded
+    form (Q8_0, Q4_0) scales each row by its own power of two, the bf16 form
+    (Q4_1) needs none; both stay within the parity bound."""
+    rng = np.random.default_rng(1000 + q)
+    rows, cols, m = 384, 1024, 70
+    w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+    s = mq.QuantizeTensor(w, q)
+    x = rng.standard_normal((m, cols)).astype(np.float32)
+    x *= (10.0 ** np.linspace(-30, 30, m)).astype(np.float32)[:, None]
+    x[5] = 0.0
+    x[9, 100] = 3.0e4 * np.abs(x[9]).max()
+    y_ref = oracle.linear(q, s.bytes, rows, cols, x, threads=THREADS)
+    bound = abs_dot_bound(oracle.dequantize(q, s.bytes, rows, cols), x)
+    got = gpu_linear(mq, s, x, cuda_device, path=0)
+    assert np.all(got[5] == 0.0)
+    assert_linear_close(got, y_ref, bound)
 
 
 def test_cta_pair_kernel_rejects_odd_tile_counts(mq, cuda_device):
