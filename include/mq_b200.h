@@ -166,8 +166,11 @@ int mq_linear_noalloc(const mq_weight *w, const float *x, int m, int ldx, const 
  * A weight of N = G*R rows is split into G equal output-row shards
  * (mq_weight_shard_create with rows [r*R, (r+1)*R) on rank r). Each rank
  * computes its R outputs and an NCCL all-gather over NVLink assembles the
- * full [m, N] output on every rank; the result is bit-identical to mq_linear
- * on the whole weight. No counterpart in the reference, which runs every
+ * full [m, N] output on every rank. The result equals mq_linear on the whole
+ * weight up to fp32 summation order: the kernels split each tile's K range
+ * across CTAs by the launch's total work, so a shard may sum in another order
+ * (bit-identical where both launches split alike, e.g. when neither has more
+ * (128-row tile, K step) chunks than SMs). No counterpart in the reference, which runs every
  * linear on one device (`--device N`, src/main.cc:249-250); new surface for
  * the multi-GPU row of the hot path. NCCL is loaded at run time
  * (libnccl.so.2). */

@@ -5,8 +5,13 @@
 // mq_weight (mq_weight_shard_create). Rows are independent (y_n = <W_n, x>),
 // so each rank computes its R outputs with the ordinary decode/prefill
 // kernels and one all-gather over NVLink assembles y [m, G*R] on every rank.
-// The result is bit-identical to the unsharded product: the same kernels see
-// the same rows.
+// Each rank runs the kernels of mq_linear on its rows. The decode and prefill
+// kernels split every tile's K range across CTAs according to the launch's
+// total work, so a shard's split, and with it the fp32 summation order, can
+// differ from the whole weight's: the gathered result then matches mq_linear
+// on the whole weight to fp32 rounding (both within the oracle's bound), and
+// is bit-identical where the two launches split K alike (for instance when
+// neither has more (tile, K step) chunks than CTAs, as in the tests).
 //
 // The gather runs over peer memory: at communicator creation every rank
 // allocates a staging region ([2 halves][nranks slots][kP2PSlotFloats] floats,

@@ -4,7 +4,10 @@ The hot path's multi-GPU form: a projection of N = G*R output rows is split
 into G equal row shards, rank r holding rows [r*R, (r+1)*R). Each rank runs
 the ordinary kernels on its shard and one NCCL all-gather over NVLink
 assembles the full output on every rank (mq_linear_sharded_allgather). Rows
-are independent, so the result is bit-identical to the unsharded product.
+are independent, so the result equals the unsharded product up to fp32
+summation order (the kernels split each tile's K range by the launch's total
+work, so a shard may sum in another order; bit-identical where both launches
+split alike, as for products with no more (tile, K step) chunks than SMs).
 
 The reference runs every linear on one device (``--device N``,
 src/main.cc:249-250); this module is new surface for the multi-GPU row.

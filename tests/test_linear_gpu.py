@@ -152,7 +152,9 @@ def test_bias_strides_and_alignment(mq, oracle, cuda_device):
 
 
 def test_sharded_rows_are_slices_of_full(mq, oracle, cuda_device):
-    """A row shard computes exactly the rows of the full matrix (bit-identical)."""
+    """A row shard computes exactly the rows of the full matrix (bit-identical:
+    at 1024 x 512 both launches give every (tile, K step) chunk its own CTA, so
+    the sums run in the same order)."""
     torch = _torch()
     for q in QTYPES:
         s, x, y_ref, bound = _llama_case(mq, oracle, q, 1024, 512, 2, seed=9 + q)
@@ -164,6 +166,34 @@ def test_sharded_rows_are_slices_of_full(mq, oracle, cuda_device):
         torch.cuda.synchronize()
         assert np.array_equal(np.concatenate(parts, axis=1).view(np.uint32), full.view(np.uint32))
         assert_linear_close(full, y_ref, bound)
+
+
+@pytest.mark.parametrize("m", [1, 16, 300], ids=["int8_decode", "folded_decode", "prefill_gemm"])
+def test_large_shards_match_full_to_rounding(mq, oracle, cuda_device, m):
+    """At Llama-3-8B FFN size the shards' launches split K differently from the
+    whole weight's (more (tile, K step) chunks than SMs), so the sums run in a
+    different order: every shard's rows must still match the full product
+    within the parity tolerance (relative to sum_k |w_nk x_mk|)."""
+    torch = _torch()
+    rng = np.random.default_rng(4242 + m)
+    rows, cols, q = 14336, 4096, Q4_0
+    w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+    s = mq.QuantizeTensor(w, q)
+    x = rng.standard_normal((m, cols)).astype(np.float32)
+    xd = dev(x, cuda_device)
+    full_w = mq.CudaWeight(s, device=cuda_device)
+    full = full_w.linear(xd).cpu().numpy()
+    full_w.close()
+    bound = abs_dot_bound(oracle.dequantize(q, s.bytes, rows, cols), x)
+    for G in (2, 8):
+        R = rows // G
+        parts = []
+        for g in range(G):
+            sh = mq.CudaWeight(s, device=cuda_device, row_range=(R * g, R * (g + 1)))
+            parts.append(sh.linear(xd).cpu().numpy())
+            sh.close()
+        torch.cuda.synchronize()
+        assert_linear_close(np.concatenate(parts, axis=1), full, bound)
 
 
 def test_ragged_offsets(mq, oracle, cuda_device):
