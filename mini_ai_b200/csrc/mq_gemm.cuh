@@ -341,10 +341,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4) {
             if constexpr (QT == MQ_Q8_0) {
-              const uint4 v = ld_stream_v4(chunk + chunk16_off(rr, 2 * q4 + (kt & 1), qd));
+              // cached in L1: the rest of each 32-byte sector is the next K step's
+              const uint4 v = __ldg(reinterpret_cast<const uint4 *>(chunk + chunk16_off(rr, 2 * q4 + (kt & 1), qd)));
               qn.w[q4][0][0] = v.x, qn.w[q4][0][1] = v.y, qn.w[q4][1][0] = v.z, qn.w[q4][1][1] = v.w;
             } else {
-              const uint2 v = ld_stream_v2(chunk + chunk16_off(rr, 4 * qd + q4, 0) + 8 * (kt & 1));
+              const uint2 v =
+                  __ldg(reinterpret_cast<const uint2 *>(chunk + chunk16_off(rr, 4 * qd + q4, 0) + 8 * (kt & 1)));
               qn.w[q4][0][0] = v.x, qn.w[q4][1][0] = v.y;
             }
           }
